@@ -1,0 +1,162 @@
+/*
+ * tinybatch_b200 — C ABI of the B200 (sm_100a) kernels for the tensor-parallel
+ * paged Qwen2 layer.
+ *
+ * Conventions
+ *   - Every pointer argument is a device pointer unless its name ends in _h.
+ *   - bf16 means IEEE bfloat16 (__nv_bfloat16), row-major, leading dimension
+ *     (ld*) in elements; weights are in F.linear layout [out, in].
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).
+ *   - Every call returns TB_OK (0) or a TB_ERR_* code; tb_last_error() gives
+ *     the message of the last failure on the calling thread.  No call
+ *     allocates device memory: scratch space ("ws") is owned by the caller.
+ *   - Split-K scratch must be zero-filled when first handed to the library;
+ *     every call leaves its arrival counters at zero again.
+ *   - Device-side problems (a bounded wait that ran out, an out-of-range
+ *     block id or position) are recorded in a device status word and read
+ *     with tb_status(); the kernel that saw them finishes without faulting.
+ *
+ * Reference interfaces (coindef/tinybatch, paths relative to its root):
+ *   src/tinybatch/model.py         Qwen2Paged.forward  :100-158
+ *   src/tinybatch/kv_cache.py      PagedKVCache.write/gather :25-45
+ *   src/tinybatch/tensor_parallel.py  tp_forward :64-117, allreduce :76-84
+ *   src/tinybatch/engine.py        LLMEngine._sample greedy argmax :149-151
+ */
+#ifndef TINYBATCH_B200_H
+#define TINYBATCH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TB_OK 0
+#define TB_ERR_ARG 1     /* invalid shape, alignment or pointer */
+#define TB_ERR_CUDA 2    /* a CUDA call failed */
+#define TB_ERR_TIMEOUT 3 /* a bounded wait (device or peer) ran out */
+#define TB_ERR_STATE 4   /* communicator not initialised / already closed */
+
+/* Device status codes (tb_status). */
+#define TB_STATUS_MBAR_TIMEOUT 101 /* a pipeline barrier wait ran out */
+#define TB_STATUS_PEER_TIMEOUT 102 /* a cross-GPU flag wait ran out */
+#define TB_STATUS_BAD_INDEX 103    /* block id / position / slot out of range */
+
+int tb_version(void);
+const char* tb_last_error(void);
+
+/* Read (and optionally clear) the device status word of the current device.
+ * Synchronises the device. */
+int tb_status(unsigned int* code_h, int clear);
+
+/* ------------------------------------------------------------------ GEMMs
+ * Common arguments of the GEMM entry points:
+ *   x [M, K] bf16 (ldx), w [N, K] bf16 (ldw): out = x . w^T, fp32 accumulate
+ *   sq, sq_parts, sq_ld, inv_d, eps: deferred RMSNorm of x.  When sq is not
+ *     NULL, row m of the product is scaled by
+ *     rsqrt(inv_d * sum_{p<sq_parts} sq[p*sq_ld + m] + eps), i.e. x holds
+ *     h * norm_weight and sq holds partial sums of h^2 — exactly
+ *     rms_norm(h) . w^T of src/tinybatch/model.py:65-69.
+ *   bn: output tile width (64, 128 or 256); splits: split-K factor;
+ *   ws/ws_bytes: split-K scratch of at least tb_gemm_scratch_bytes(M, N, bn,
+ *     splits) bytes (arrival counters, then fp32 partial tiles); unused and
+ *     may be NULL when splits == 1.
+ */
+size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits);
+
+/* Plain projection: out = rowscale * x . w^T, fp32 (out_f32=1) or bf16.
+ * Replaces F.linear of the LM head (src/tinybatch/model.py:158,
+ * tensor_parallel.py:117). */
+int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
+              const float* sq, int sq_parts, int sq_ld, float inv_d, float eps,
+              void* out, int ld_out, int out_f32, int bn, int splits,
+              void* ws, size_t ws_bytes, void* stream);
+
+/* Column-parallel fused QKV projection.  w_qkv = [Wq; Wk; Wv] of this rank's
+ * heads ([(Hq+2Hkv)*hd, K]), bias likewise.  Epilogue: rowscale, + bias,
+ * NeoX RoPE of q and k with the fp32 tables rope_cos/rope_sin
+ * [max_pos, hd/2], q -> q_out [M, Hq*hd]; k, v -> kv_pool
+ * [num_blocks, 2, Hkv, block_size, hd] at flat slot slots[m]
+ * (= block*block_size + offset).
+ * Replaces q/k/v F.linear + _rope + PagedKVCache.write
+ * (src/tinybatch/model.py:119-128, kv_cache.py:25-38,
+ *  tensor_parallel.py:92-97).  bn must be a multiple of hd. */
+int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const void* bias,
+                   int M, int K, int n_q_heads, int n_kv_heads, int head_dim,
+                   const float* sq, int sq_parts, int sq_ld, float inv_d, float eps,
+                   const float* rope_cos, const float* rope_sin, int max_pos,
+                   const int* positions, const int* slots,
+                   void* q_out, int ld_q, void* kv_pool, int block_size,
+                   int bn, int splits, void* ws, size_t ws_bytes, void* stream);
+
+/* Column-parallel gate/up projection with SwiGLU epilogue.  w_gu holds, for
+ * each output tile t of width bn, the bn/2 gate rows of features
+ * [t*bn/2, (t+1)*bn/2) followed by the matching bn/2 up rows (zero rows pad
+ * the last tile).  act [M, n_feat] = silu(g) * u.
+ * Replaces gate/up F.linear + F.silu(gate)*up (src/tinybatch/model.py:152-154,
+ * tensor_parallel.py:111-114). */
+int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, int K,
+                      int n_feat, const float* sq, int sq_parts, int sq_ld, float inv_d,
+                      float eps, void* act, int ld_act, int bn, int splits,
+                      void* ws, size_t ws_bytes, void* stream);
+
+/* Row-parallel projection + residual + next-norm prologue, single rank:
+ *   h[m, :] += x . w^T  (fp32 residual stream, in place)
+ *   hg = bf16(h * g_next), sq_out[tile_n, m] = sum over the tile's columns of h^2
+ * so the next GEMM applies rms_norm(h) * g_next through its rowscale.
+ * Optional gather: when row_dst is not NULL and row_dst[m] >= 0, row m of hg
+ * and of sq_out is also written to row row_dst[m] of hg2 / sq2.
+ * Replaces h + F.linear(attn, Wo) / h + F.linear(act, Wd) and the following
+ * _rms_norm (src/tinybatch/model.py:149-151,154,156; tensor_parallel.py:108-110,114,116).
+ * The number of sq parts written is ceil(N / bn). */
+int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
+                           float* h, int ld_h, const void* g_next, void* hg, int ld_hg,
+                           float* sq_out, int sq_out_ld, const int* row_dst, void* hg2,
+                           float* sq2, int sq2_ld, int bn, int splits, void* ws,
+                           size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------- attention
+ * Paged GQA attention reading K/V through block tables (no gather copy).
+ *   q [*, Hq*hd] bf16 (ld_q), out [*, Hq*hd] bf16 (ld_out)
+ *   block_tables [n_seqs, bt_ld] int32, q_start/q_len/ctx_len [n_seqs] int32
+ * Sequence s has query rows q_start[s] .. +q_len[s]; its query token i sits at
+ * position ctx_len[s]-q_len[s]+i and attends to keys 0..that position.
+ * Replaces PagedKVCache.gather + repeat_interleave + SDPA
+ * (src/tinybatch/model.py:131-147, kv_cache.py:40-45, tensor_parallel.py:99-105).
+ *
+ * _decode: every sequence must have q_len*Hq/Hkv <= 16 (decode steps).
+ *   Keys are split into pieces of split_tokens (a multiple of 16); grid is
+ *   sized for max_ctx.  Scratch: tb_attention_scratch_bytes.
+ * _prefill: any q_len; work_pairs [n_work, 2] int32 = (seq, 64-row tile). */
+size_t tb_attention_scratch_bytes(int n_seqs, int n_kv_heads, int head_dim, int max_ctx,
+                                  int split_tokens);
+int tb_paged_attention_decode(const void* q, int ld_q, void* out, int ld_out,
+                              const void* kv_pool, int num_blocks, int n_q_heads,
+                              int n_kv_heads, int head_dim, int block_size,
+                              const int* block_tables, int bt_ld, const int* q_start,
+                              const int* q_len, const int* ctx_len, int n_seqs, int max_ctx,
+                              int split_tokens, void* ws, size_t ws_bytes, void* stream);
+int tb_paged_attention_prefill(const void* q, int ld_q, void* out, int ld_out,
+                               const void* kv_pool, int num_blocks, int n_q_heads,
+                               int n_kv_heads, int head_dim, int block_size,
+                               const int* block_tables, int bt_ld, const int* q_start,
+                               const int* q_len, const int* ctx_len, int n_seqs,
+                               const int* work_pairs, int n_work, void* stream);
+
+/* ------------------------------------------------------ embedding, sampling */
+
+/* h[m] = float(emb[ids[m]]); hg = bf16(h * g); sq[m] = sum h^2 (one part).
+ * Replaces F.embedding + the first _rms_norm (src/tinybatch/model.py:112,116). */
+int tb_embed(const int* ids, int M, const void* emb, int ld_emb, int d, int vocab,
+             const void* g, float* h, int ld_h, void* hg, int ld_hg, float* sq, void* stream);
+
+/* out[m] = argmax_n logits[m, n] (first maximal index), logits fp32.
+ * Replaces the greedy branch of LLMEngine._sample (src/tinybatch/engine.py:149-151). */
+int tb_argmax(const float* logits, int ld, int M, int N, int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TINYBATCH_B200_H */

@@ -1,0 +1,486 @@
+// Paged GQA attention that reads K/V straight from the block pool.
+//
+// Pool layout (unchanged from the reference): [num_blocks, 2, n_kv, bs, hd]
+// bf16, K at index 0 and V at 1; token at position p of a sequence lives in
+// block table[p / bs], slot p % bs.
+//
+// Rows.  For one (sequence, kv head) the query rows are the pairs
+// (query token i, head g in the kv head's group of G = Hq/Hkv heads), row
+// r = i*G + g.  Query token i sits at absolute position ctx - q_len + i and
+// sees keys 0 .. ctx - q_len + i (causal with a cached prefix).
+//
+// Math.  S = Q K^T and O = P V run on mma.sync m16n8k16 (bf16 in, fp32
+// accumulate) over 16-token key chunks staged in shared memory with
+// cp.async (16-byte pieces, XOR-swizzled so ldmatrix is conflict-free);
+// softmax is the online (running max / running sum) form in base 2.
+//
+//   decode kernel   q_len*G <= 16 rows; one CTA per (split, kv head, seq);
+//                   the 4 warps take interleaved key chunks of the split and
+//                   merge their (max, sum, O) in shared memory; with more
+//                   than one split the CTA writes (O/l, log2 l + max) and
+//                   attn_combine_kernel merges the splits.
+//   prefill kernel  64 rows per CTA (16 per warp), key chunks shared by the
+//                   4 warps, causal limit per row.
+#include "attention.cuh"
+#include "common.cuh"
+#include "host.h"
+
+namespace tb {
+
+
+
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(pred ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 16-token chunk of K (or V) for one kv head: [16][HD] bf16, 16-byte pieces
+// XOR-swizzled within each row.
+template <int HD>
+struct ChunkLayout {
+  static constexpr int CPR = HD / 8;                   // 16-byte pieces per row
+  static constexpr int XM = (CPR < 8 ? CPR : 8) - 1;  // swizzle mask
+  static constexpr int BYTES = 16 * HD * 2;
+  __device__ static __forceinline__ int off(int t, int c) { return t * HD * 2 + ((c ^ (t & XM)) << 4); }
+};
+
+// Issue the cp.async pieces of key chunk `chunk` (K and V) handled by this
+// thread (thread `tid` of `nthr`).
+template <int HD>
+__device__ __forceinline__ void load_chunk(const AttnArgs& a, const int* table, int kvh, int ctx,
+                                           int chunk, uint32_t sk, uint32_t sv, int tid, int nthr) {
+  using C = ChunkLayout<HD>;
+  const size_t head_stride = (size_t)a.block_size * HD;
+  for (int i = tid; i < 16 * C::CPR; i += nthr) {
+    const int t = i / C::CPR, c = i % C::CPR;
+    const int p = chunk * 16 + t;
+    bool ok = p < ctx;
+    const __nv_bfloat16* src = a.pool;
+    if (ok) {
+      const int blk = table[p / a.block_size];
+      if (blk < 0 || blk >= a.num_blocks) {
+        set_status(ERR_BAD_INDEX);
+        ok = false;
+      } else {
+        src = a.pool + ((size_t)blk * 2 * a.n_kv_heads + kvh) * head_stride +
+              (size_t)(p % a.block_size) * HD + c * 8;
+      }
+    }
+    cp_async16(sk + C::off(t, c), src, ok);
+    cp_async16(sv + C::off(t, c), ok ? src + (size_t)a.n_kv_heads * head_stride : src, ok);
+  }
+}
+
+// Per-warp flash state for 16 rows: thread holds rows lane/4 and lane/4+8.
+template <int HD>
+struct Flash {
+  float o[HD / 8][4];
+  float m[2], l[2];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    m[0] = m[1] = -INFINITY;
+    l[0] = l[1] = 0.f;
+  }
+
+  // One 16-key chunk.  qa: A fragments of Q; `limit[h]` = last key position
+  // row-half h may see (inclusive); keys >= ctx are masked too.
+  __device__ __forceinline__ void step(const uint32_t (*qa)[4], uint32_t sk, uint32_t sv,
+                                       int chunk, int ctx, const int* limit, float scale_log2,
+                                       int lane) {
+    using C = ChunkLayout<HD>;
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t b[4];
+      const int tok = (mi >> 1) * 8 + rr;
+      ldsm_x4(sk + C::off(tok, ks * 2 + (mi & 1)), b);
+      mma16816(s[0], qa[ks], b[0], b[1]);
+      mma16816(s[1], qa[ks], b[2], b[3]);
+    }
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const int p = chunk * 16 + nt * 8 + 2 * (lane & 3) + (e & 1);
+        float v = s[nt][e] * scale_log2;
+        if (p >= ctx || p > limit[h]) v = -INFINITY;
+        s[nt][e] = v;
+        mx[h] = fmaxf(mx[h], v);
+      }
+    float alpha[2], mu[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      const float mn = fmaxf(m[h], mx[h]);
+      mu[h] = mn == -INFINITY ? 0.f : mn;
+      alpha[h] = exp2f(m[h] - mu[h]);
+      m[h] = mn;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = exp2f(s[nt][e] - mu[e >> 1]);
+        s[nt][e] = p;
+        rs[e >> 1] += p;
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) l[h] = l[h] * alpha[h] + rs[h];
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) {
+      o[i][0] *= alpha[0];
+      o[i][1] *= alpha[0];
+      o[i][2] *= alpha[1];
+      o[i][3] *= alpha[1];
+    }
+    uint32_t pa[4];
+    pa[0] = pack_bf16x2(s[0][0], s[0][1]);
+    pa[1] = pack_bf16x2(s[0][2], s[0][3]);
+    pa[2] = pack_bf16x2(s[1][0], s[1][1]);
+    pa[3] = pack_bf16x2(s[1][2], s[1][3]);
+#pragma unroll
+    for (int dt = 0; dt < HD / 16; ++dt) {
+      uint32_t b[4];
+      const int tok = (mi & 1) * 8 + rr;
+      ldsm_x4_t(sv + C::off(tok, dt * 2 + (mi >> 1)), b);
+      mma16816(o[2 * dt], pa, b[0], b[1]);
+      mma16816(o[2 * dt + 1], pa, b[2], b[3]);
+    }
+  }
+
+  __device__ __forceinline__ void finish_sum() {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+      l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+    }
+  }
+};
+
+// A fragments of 16 query rows (rows >= nrows are zero).
+template <int HD>
+__device__ __forceinline__ void load_q(const AttnArgs& a, int q0, int G, int kvh, int row0,
+                                       int nrows, int lane, uint32_t (*qa)[4]) {
+  const int g4 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int r = row0 + g4 + half * 8;
+    const bool ok = (r - row0) < nrows;
+    const __nv_bfloat16* src =
+        ok ? a.q + (size_t)(q0 + r / G) * a.ld_q + (size_t)(kvh * G + r % G) * HD : a.q;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t lo = 0, hi = 0;
+      if (ok) {
+        lo = *reinterpret_cast<const uint32_t*>(src + ks * 16 + 2 * t4);
+        hi = *reinterpret_cast<const uint32_t*>(src + ks * 16 + 8 + 2 * t4);
+      }
+      qa[ks][half] = lo;
+      qa[ks][2 + half] = hi;
+    }
+  }
+}
+
+constexpr int DEC_STAGES = 3;
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
+  using C = ChunkLayout<HD>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
+  const int G = a.n_q_heads / a.n_kv_heads;
+  const int nrows = qlen * G;
+  const int n_chunks = (ctx + 15) / 16;
+  const int n_splits = (n_chunks + a.split_chunks - 1) / a.split_chunks;
+  if (split >= n_splits || nrows <= 0) return;
+  if (nrows > 16) {
+    set_status(ERR_BAD_INDEX);
+    return;
+  }
+  const int c_begin = split * a.split_chunks;
+  const int c_end = min(c_begin + a.split_chunks, n_chunks);
+  const int* table = a.block_tables + (size_t)seq * a.bt_ld;
+
+  uint32_t qa[HD / 16][4];
+  load_q<HD>(a, q0, G, kvh, 0, nrows, lane, qa);
+  int limit[2];
+  {
+    const int first = ctx - qlen;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = min((lane >> 2) + 8 * h, nrows - 1);
+      limit[h] = first + r / G;
+    }
+  }
+
+  const uint32_t ring = smem_u32(smem) + warp * DEC_STAGES * 2 * C::BYTES;
+  Flash<HD> f;
+  f.init();
+  // this warp's chunks: c_begin + warp + 4*j
+  const int my_n = c_end - c_begin - warp > 0 ? (c_end - c_begin - warp + 3) / 4 : 0;
+#pragma unroll
+  for (int j = 0; j < DEC_STAGES - 1; ++j) {
+    if (j < my_n) {
+      const uint32_t st = ring + j * 2 * C::BYTES;
+      load_chunk<HD>(a, table, kvh, ctx, c_begin + warp + 4 * j, st, st + C::BYTES, lane, 32);
+    }
+    cp_commit();
+  }
+  for (int j = 0; j < my_n; ++j) {
+    cp_wait<DEC_STAGES - 2>();
+    __syncwarp();
+    const uint32_t st = ring + (j % DEC_STAGES) * 2 * C::BYTES;
+    f.step(qa, st, st + C::BYTES, c_begin + warp + 4 * j, ctx, limit, a.scale_log2, lane);
+    __syncwarp();
+    const int jn = j + DEC_STAGES - 1;
+    if (jn < my_n) {
+      const uint32_t sn = ring + (jn % DEC_STAGES) * 2 * C::BYTES;
+      load_chunk<HD>(a, table, kvh, ctx, c_begin + warp + 4 * jn, sn, sn + C::BYTES, lane, 32);
+    }
+    cp_commit();
+  }
+  cp_wait<0>();
+  f.finish_sum();
+  __syncthreads();
+
+  // merge the 4 warps: smem reused as O[4][16][HD], m[4][16], l[4][16]
+  float* so = reinterpret_cast<float*>(smem);
+  float* sm = so + 4 * 16 * HD;
+  float* sl = sm + 4 * 16;
+  {
+    const int g4 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = g4 + (e >> 1) * 8, c = nt * 8 + 2 * t4 + (e & 1);
+        so[(warp * 16 + r) * HD + c] = f.o[nt][e];
+      }
+    if (t4 == 0) {
+      sm[warp * 16 + g4] = f.m[0];
+      sm[warp * 16 + g4 + 8] = f.m[1];
+      sl[warp * 16 + g4] = f.l[0];
+      sl[warp * 16 + g4 + 8] = f.l[1];
+    }
+  }
+  __syncthreads();
+  const bool direct = n_splits == 1;
+  for (int i = threadIdx.x; i < nrows * HD; i += blockDim.x) {
+    const int r = i / HD, c = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
+    const float mu = M == -INFINITY ? 0.f : M;
+    float L = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float sc = exp2f(sm[w * 16 + r] - mu);
+      L += sl[w * 16 + r] * sc;
+      acc += so[(w * 16 + r) * HD + c] * sc;
+    }
+    const float val = L > 0.f ? acc / L : 0.f;
+    if (direct) {
+      a.out[(size_t)(q0 + r / G) * a.ld_out + (size_t)(kvh * G + r % G) * HD + c] =
+          __float2bfloat16_rn(val);
+    } else {
+      const size_t base = (((size_t)seq * a.n_kv_heads + kvh) * a.max_splits + split) * 16 + r;
+      a.ws_o[base * HD + c] = val;
+      if (c == 0) a.ws_lse[base] = L > 0.f ? mu + log2f(L) : -INFINITY;
+    }
+  }
+}
+
+// Merge decode splits: one CTA per (kv head, seq); skips sequences that fit
+// one split (their output was written directly).
+template <int HD>
+__global__ void attn_combine_kernel(const AttnArgs a) {
+  const int kvh = blockIdx.x, seq = blockIdx.y;
+  const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
+  const int G = a.n_q_heads / a.n_kv_heads;
+  const int nrows = qlen * G;
+  const int n_chunks = (ctx + 15) / 16;
+  const int n_splits = (n_chunks + a.split_chunks - 1) / a.split_chunks;
+  if (n_splits <= 1 || nrows > 16) return;
+  const size_t base0 = ((size_t)seq * a.n_kv_heads + kvh) * a.max_splits;
+  for (int i = threadIdx.x; i < nrows * HD; i += blockDim.x) {
+    const int r = i / HD, c = i % HD;
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, a.ws_lse[(base0 + s) * 16 + r]);
+    const float mu = M == -INFINITY ? 0.f : M;
+    float W = 0.f, acc = 0.f;
+    for (int s = 0; s < n_splits; ++s) {
+      const float w = exp2f(a.ws_lse[(base0 + s) * 16 + r] - mu);
+      W += w;
+      acc += w * a.ws_o[((base0 + s) * 16 + r) * HD + c];
+    }
+    a.out[(size_t)(q0 + r / G) * a.ld_out + (size_t)(kvh * G + r % G) * HD + c] =
+        __float2bfloat16_rn(W > 0.f ? acc / W : 0.f);
+  }
+}
+
+constexpr int PF_STAGES = 2;
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
+  using C = ChunkLayout<HD>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int seq = a.work[2 * blockIdx.x], rt = a.work[2 * blockIdx.x + 1];
+  const int kvh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
+  const int G = a.n_q_heads / a.n_kv_heads;
+  const int nrows_total = qlen * G;
+  const int row0 = rt * 64 + warp * 16;
+  const int nrows = max(0, min(16, nrows_total - row0));
+  const int first = ctx - qlen;
+  const int* table = a.block_tables + (size_t)seq * a.bt_ld;
+  // keys needed by the whole CTA: up to the last row's causal limit
+  const int last_row = min(rt * 64 + 63, nrows_total - 1);
+  const int cta_keys = min(ctx, first + last_row / G + 1);
+  const int n_chunks = (cta_keys + 15) / 16;
+
+  uint32_t qa[HD / 16][4];
+  load_q<HD>(a, q0, G, kvh, row0, nrows, lane, qa);
+  int limit[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = row0 + min((lane >> 2) + 8 * h, max(nrows - 1, 0));
+    limit[h] = first + r / G;
+  }
+  const int warp_keys = nrows > 0 ? min(ctx, first + (row0 + nrows - 1) / G + 1) : 0;
+
+  const uint32_t ring = smem_u32(smem);
+  Flash<HD> f;
+  f.init();
+  if (n_chunks > 0) load_chunk<HD>(a, table, kvh, ctx, 0, ring, ring + C::BYTES, threadIdx.x, 128);
+  cp_commit();
+  for (int ci = 0; ci < n_chunks; ++ci) {
+    if (ci + 1 < n_chunks) {
+      const uint32_t sn = ring + ((ci + 1) % PF_STAGES) * 2 * C::BYTES;
+      load_chunk<HD>(a, table, kvh, ctx, ci + 1, sn, sn + C::BYTES, threadIdx.x, 128);
+    }
+    cp_commit();
+    cp_wait<1>();
+    __syncthreads();
+    const uint32_t st = ring + (ci % PF_STAGES) * 2 * C::BYTES;
+    if (ci * 16 < warp_keys) f.step(qa, st, st + C::BYTES, ci, ctx, limit, a.scale_log2, lane);
+    __syncthreads();
+  }
+  cp_wait<0>();
+  f.finish_sum();
+  const int g4 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = g4 + 8 * h;
+    if (r >= nrows) continue;
+    const int R = row0 + r;
+    const float inv = f.l[h] > 0.f ? 1.f / f.l[h] : 0.f;
+    __nv_bfloat16* dst = a.out + (size_t)(q0 + R / G) * a.ld_out + (size_t)(kvh * G + R % G) * HD;
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; ++nt) {
+      const int c = nt * 8 + 2 * t4;
+      *reinterpret_cast<uint32_t*>(dst + c) =
+          pack_bf16x2(f.o[nt][2 * h] * inv, f.o[nt][2 * h + 1] * inv);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <int HD>
+static int decode_launch(const AttnArgs& a, cudaStream_t st) {
+  const int smem_ring = 4 * DEC_STAGES * 2 * ChunkLayout<HD>::BYTES;
+  const int smem_merge = (4 * 16 * HD + 2 * 4 * 16) * 4;
+  const int smem = smem_ring > smem_merge ? smem_ring : smem_merge;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return host_err(e, "attention smem attribute");
+    attr = true;
+  }
+  dim3 grid(a.max_splits, a.n_kv_heads, a.n_seqs);
+  attn_decode_kernel<HD><<<grid, 128, smem, st>>>(a);
+  int rc = host_err(cudaGetLastError(), "attention decode launch");
+  if (rc || a.max_splits <= 1) return rc;
+  attn_combine_kernel<HD><<<dim3(a.n_kv_heads, a.n_seqs), 128, 0, st>>>(a);
+  return host_err(cudaGetLastError(), "attention combine launch");
+}
+
+template <int HD>
+static int prefill_launch(const AttnArgs& a, int n_work, cudaStream_t st) {
+  const int smem = PF_STAGES * 2 * ChunkLayout<HD>::BYTES;
+  attn_prefill_kernel<HD><<<dim3(n_work, a.n_kv_heads), 128, smem, st>>>(a);
+  return host_err(cudaGetLastError(), "attention prefill launch");
+}
+
+static int check_common(const AttnArgs& a, int head_dim) {
+  if (a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads) return arg_err("heads: Hq % Hkv != 0");
+  if (a.block_size <= 0 || a.num_blocks <= 0) return arg_err("block_size / num_blocks");
+  if ((a.ld_q % 8) || (a.ld_out % 8)) return arg_err("ld_q / ld_out must be multiples of 8");
+  if (head_dim != 16 && head_dim != 64 && head_dim != 128) return arg_err("head_dim must be 16, 64 or 128");
+  return TB_OK;
+}
+
+int attn_decode(AttnArgs a, int head_dim, cudaStream_t st) {
+  int rc = check_common(a, head_dim);
+  if (rc) return rc;
+  if (a.n_q_heads / a.n_kv_heads > 16) return arg_err("GQA group larger than 16");
+  if (a.split_chunks <= 0 || a.max_splits <= 0) return arg_err("split sizes");
+  if (a.max_splits > 1 && (a.ws_o == nullptr || a.ws_lse == nullptr)) return arg_err("split workspace");
+  if (a.n_seqs == 0) return TB_OK;
+  a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  switch (head_dim) {
+    case 16: return decode_launch<16>(a, st);
+    case 64: return decode_launch<64>(a, st);
+    default: return decode_launch<128>(a, st);
+  }
+}
+
+int attn_prefill(AttnArgs a, int head_dim, int n_work, cudaStream_t st) {
+  int rc = check_common(a, head_dim);
+  if (rc) return rc;
+  if (n_work == 0) return TB_OK;
+  a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  switch (head_dim) {
+    case 16: return prefill_launch<16>(a, n_work, st);
+    case 64: return prefill_launch<64>(a, n_work, st);
+    default: return prefill_launch<128>(a, n_work, st);
+  }
+}
+
+}  // namespace tb

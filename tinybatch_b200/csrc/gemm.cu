@@ -1,0 +1,421 @@
+// tcgen05 GEMM kernel and its host launcher (see gemm.cuh for the design).
+#include <stdio.h>
+
+#include "gemm.cuh"
+#include "host.h"
+
+namespace tb {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN, int STAGES>
+struct GemmLayout {
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = STAGES * A_BYTES;
+  static constexpr int OFF_BAR = OFF_B + STAGES * B_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 1) * 8 + 16;
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ float row_scale(const GemmArgs& g, int m) {
+  if (g.sq == nullptr || m >= g.M) return 1.f;
+  float s = 0.f;
+  for (int p = 0; p < g.sq_parts; ++p) s += g.sq[(size_t)p * g.sq_ld + m];
+  return rsqrtf(s * g.inv_d + g.eps);
+}
+
+// Accumulator access for the epilogue: columns [c, c+W) of this thread's row.
+// Collective over the warp (tcgen05.ld is .sync.aligned): every lane calls it.
+template <int BN>
+struct AccReader {
+  uint32_t taddr;   // TMEM address of this warp's lane quarter, column 0
+  int splits, z, row;
+  const float* ws;  // this tile's workspace, [splits][BN][128]
+  template <int W>
+  __device__ __forceinline__ void load(int c, float* v) const {
+    float own[W];
+    if constexpr (W == 16) tmem_ld16(taddr + c, own);
+    else tmem_ld8(taddr + c, own);
+    if (splits == 1) {
+#pragma unroll
+      for (int j = 0; j < W; ++j) v[j] = own[j];
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) v[j] = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      if (s == z) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] += own[j];
+      } else {
+        const float* p = ws + ((size_t)s * BN + c) * BM + row;
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] += __ldcg(p + (size_t)j * BM);
+      }
+    }
+  }
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int BN, int EPI>
+__device__ __forceinline__ void run_epilogue(const GemmArgs& g, const AccReader<BN>& acc,
+                                             int tm, int tn, int row) {
+  const int m = tm * BM + row;
+  const bool valid = m < g.M;
+  const float rs = row_scale(g, m);
+
+  if constexpr (EPI == EPI_F32 || EPI == EPI_BF16) {
+    for (int c = 0; c < BN; c += 16) {
+      const int n = tn * BN + c;
+      if (n >= g.N) break;
+      float v[16];
+      acc.template load<16>(c, v);
+      if (!valid) continue;
+      if constexpr (EPI == EPI_F32) {
+        float* o = reinterpret_cast<float*>(g.out) + (size_t)m * g.ld_out + n;
+        if (n + 16 <= g.N) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *reinterpret_cast<float4*>(o + j) =
+                make_float4(v[j] * rs, v[j + 1] * rs, v[j + 2] * rs, v[j + 3] * rs);
+        } else {
+          for (int j = 0; j < 16 && n + j < g.N; ++j) o[j] = v[j] * rs;
+        }
+      } else {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + n;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] *= rs;
+        if (n + 16 <= g.N) {
+          store_bf16x8(o, v);
+          store_bf16x8(o + 8, v + 8);
+        } else {
+          for (int j = 0; j < 16 && n + j < g.N; ++j) o[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // Tile tn holds features [tn*BN/2, (tn+1)*BN/2): gate rows first, up rows second.
+    constexpr int HALF = BN / 2;
+    for (int c = 0; c < HALF; c += 16) {
+      const int f = tn * HALF + c;
+      if (f >= g.n_feat) break;
+      float gv[16], uv[16];
+      acc.template load<16>(c, gv);
+      acc.template load<16>(HALF + c, uv);
+      if (!valid) continue;
+      float y[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float a = gv[j] * rs, b = uv[j] * rs;
+        y[j] = a / (1.f + __expf(-a)) * b;
+      }
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + f;
+      store_bf16x8(o, y);
+      store_bf16x8(o + 8, y + 8);
+    }
+  } else if constexpr (EPI == EPI_RESID) {
+    float ss = 0.f;
+    const int dst = (valid && g.row_dst != nullptr) ? g.row_dst[m] : -1;
+    for (int c = 0; c < BN; c += 16) {
+      const int n = tn * BN + c;
+      if (n >= g.N) break;
+      float v[16];
+      acc.template load<16>(c, v);
+      if (!valid) continue;
+      float* hp = g.h + (size_t)m * g.ld_h + n;
+      float gw[16], hv[16];
+      load_bf16x8(g.gnext + n, gw);
+      load_bf16x8(g.gnext + n + 8, gw + 8);
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        float4 x = *reinterpret_cast<const float4*>(hp + j);
+        x.x += v[j];
+        x.y += v[j + 1];
+        x.z += v[j + 2];
+        x.w += v[j + 3];
+        *reinterpret_cast<float4*>(hp + j) = x;
+        hv[j] = x.x;
+        hv[j + 1] = x.y;
+        hv[j + 2] = x.z;
+        hv[j + 3] = x.w;
+      }
+      float o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        ss += hv[j] * hv[j];
+        o[j] = hv[j] * gw[j];
+      }
+      __nv_bfloat16* hgp = g.hg + (size_t)m * g.ld_hg + n;
+      store_bf16x8(hgp, o);
+      store_bf16x8(hgp + 8, o + 8);
+      if (dst >= 0) {
+        __nv_bfloat16* p2 = g.hg2 + (size_t)dst * g.ld_hg + n;
+        store_bf16x8(p2, o);
+        store_bf16x8(p2 + 8, o + 8);
+      }
+    }
+    if (valid) {
+      g.sq_out[(size_t)tn * g.sq_out_ld + m] = ss;
+      if (dst >= 0) g.sq2[(size_t)tn * g.sq2_ld + dst] = ss;
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    const int hd = g.head_dim, half = hd >> 1;
+    const int heads_in_tile = BN / hd;
+    const int total_heads = g.n_q_heads + 2 * g.n_kv_heads;
+    int pos = 0, slot = 0;
+    if (valid) {
+      pos = g.positions[m];
+      slot = g.slots[m];
+      if (pos < 0 || pos >= g.max_pos || slot < 0) {
+        set_status(ERR_BAD_INDEX);
+        pos = 0;
+        slot = -1;
+      }
+    }
+    const int blk = slot >= 0 ? slot / g.block_size : 0;
+    const int off = slot >= 0 ? slot % g.block_size : 0;
+    for (int hh = 0; hh < heads_in_tile; ++hh) {
+      const int head = tn * heads_in_tile + hh;
+      if (head >= total_heads) break;
+      const int c0 = hh * hd;
+      const int n0 = head * hd;
+      __nv_bfloat16* dst;
+      bool rotate = true;
+      if (head < g.n_q_heads) {
+        dst = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + (size_t)head * hd;
+      } else {
+        const int is_v = head >= g.n_q_heads + g.n_kv_heads;
+        const int kvh = head - g.n_q_heads - (is_v ? g.n_kv_heads : 0);
+        rotate = !is_v;
+        dst = g.kv_pool +
+              ((((size_t)blk * 2 + is_v) * g.n_kv_heads + kvh) * g.block_size + off) * hd;
+      }
+      const bool store = valid && (slot >= 0 || head < g.n_q_heads);
+      if (rotate) {
+        for (int j = 0; j < half; j += 8) {
+          float lo[8], hi[8], bl[8], bh[8];
+          acc.template load<8>(c0 + j, lo);
+          acc.template load<8>(c0 + half + j, hi);
+          if (!store) continue;
+          load_bf16x8(g.bias + n0 + j, bl);
+          load_bf16x8(g.bias + n0 + half + j, bh);
+          const float* cs = g.rope_cos + (size_t)pos * half + j;
+          const float* sn = g.rope_sin + (size_t)pos * half + j;
+          float ol[8], oh[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float x1 = lo[t] * rs + bl[t], x2 = hi[t] * rs + bh[t];
+            const float c = cs[t], s = sn[t];
+            ol[t] = x1 * c - x2 * s;
+            oh[t] = x2 * c + x1 * s;
+          }
+          store_bf16x8(dst + j, ol);
+          store_bf16x8(dst + half + j, oh);
+        }
+      } else {
+        for (int j = 0; j < hd; j += 8) {
+          float x[8], b[8];
+          acc.template load<8>(c0 + j, x);
+          if (!store) continue;
+          load_bf16x8(g.bias + n0 + j, b);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) x[t] = x[t] * rs + b[t];
+          store_bf16x8(dst + j, x);
+        }
+      }
+    }
+  }
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
+                   const __grid_constant__ CUtensorMap tma_b, const GemmArgs g) {
+  using L = GemmLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem + L::OFF_A;
+  uint8_t* sB = smem + L::OFF_B;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // grouped raster: m fastest inside a group of group_m row tiles
+  const int tile = blockIdx.x;
+  const int per_group = g.group_m * g.tiles_n;
+  const int first_m = (tile / per_group) * g.group_m;
+  const int gsize = min(g.tiles_m - first_m, g.group_m);
+  const int tm = first_m + (tile % per_group) % gsize;
+  const int tn = (tile % per_group) / gsize;
+  const int z = blockIdx.y;
+  const int num_k = (g.K + BK - 1) / BK;
+  const int kb = (int)((long long)z * num_k / g.splits);
+  const int ke = (int)((long long)(z + 1) * num_k / g.splits);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer
+    for (int it = kb; it < ke; ++it) {
+      const int i = it - kb, s = i % STAGES;
+      if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) break;
+      mbar_arrive_expect_tx(&full[s], A_BYTES + L::B_BYTES);
+      tma_load_2d(sA + s * A_BYTES, &tma_a, &full[s], it * BK, tm * BM);
+      tma_load_2d(sB + s * L::B_BYTES, &tma_b, &full[s], it * BK, tn * BN);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc = idesc_bf16_m128(BN);
+    bool ok = true;
+    for (int it = kb; it < ke; ++it) {
+      const int i = it - kb, s = i % STAGES;
+      if (!mbar_wait(&full[s], (i / STAGES) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * L::B_BYTES);
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk)
+        tc_mma_bf16(tmem_base, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+      tc_commit(&empty[s]);
+    }
+    if (ok) tc_commit(done);
+    else mbar_arrive(done);
+  } else if (warp >= 2) {
+    // ---------------- epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    mbar_wait(done, 0);
+    tc_fence_after();
+    AccReader<BN> acc;
+    acc.taddr = tmem_base + ((uint32_t)(q * 32) << 16);
+    acc.splits = g.splits;
+    acc.z = z;
+    acc.row = row;
+    acc.ws = nullptr;
+    bool run = true;
+    if (g.splits > 1) {
+      const size_t tile_lin = (size_t)tm * g.tiles_n + tn;
+      float* ws_tile = g.ws + tile_lin * g.splits * BN * BM;
+      float* mine = ws_tile + (size_t)z * BN * BM + row;
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(acc.taddr + c, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) __stcg(mine + (size_t)(c + j) * BM, v[j]);
+      }
+      __threadfence();
+      epi_bar();
+      if (threadIdx.x == 64) {
+        const int prev = atomicAdd(&g.counters[tile_lin], 1);
+        const int last = prev == g.splits - 1;
+        if (last) g.counters[tile_lin] = 0;
+        *last_flag = last;
+      }
+      epi_bar();
+      run = *last_flag != 0;
+      __threadfence();
+      acc.ws = ws_tile;
+    }
+    if (run) run_epilogue<BN, EPI>(g, acc, tm, tn, row);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, BN);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <int BN, int STAGES, int EPI>
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const GemmArgs& g,
+                     cudaStream_t stream) {
+  using L = GemmLayout<BN, STAGES>;
+  auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) return host_err(e, "gemm smem attribute");
+    attr_set = true;
+  }
+  dim3 grid(g.tiles_m * g.tiles_n, g.splits);
+  kern<<<grid, GEMM_THREADS, L::SMEM, stream>>>(ta, tb_, g);
+  return host_err(cudaGetLastError(), "gemm launch");
+}
+
+template <int EPI>
+static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_, const GemmArgs& g,
+                      cudaStream_t stream) {
+  switch (bn) {
+    case 64: return launch_bn<64, 8, EPI>(ta, tb_, g, stream);
+    case 128: return launch_bn<128, 6, EPI>(ta, tb_, g, stream);
+    case 256: return launch_bn<256, 4, EPI>(ta, tb_, g, stream);
+    default: return TB_ERR_ARG;
+  }
+}
+
+int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb, GemmArgs g,
+                cudaStream_t stream) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return TB_ERR_ARG;
+  if ((lda * 2) % 16 || (ldb * 2) % 16 || lda < g.K || ldb < g.K) return TB_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(A) % 16 || reinterpret_cast<uintptr_t>(B) % 16) return TB_ERR_ARG;
+  const int num_k = (g.K + BK - 1) / BK;
+  if (g.splits < 1 || g.splits > num_k) return TB_ERR_ARG;
+  if (g.splits > 1 && (g.ws == nullptr || g.counters == nullptr)) return TB_ERR_ARG;
+  g.tiles_m = (g.M + BM - 1) / BM;
+  g.tiles_n = (g.N + bn - 1) / bn;
+  if (g.group_m <= 0) g.group_m = 16;
+  CUtensorMap ta, tbm;
+  int rc = make_tmap_2d(&ta, A, g.K, g.M, (uint64_t)lda * 2, BK, BM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tbm, B, g.K, g.N, (uint64_t)ldb * 2, BK, bn);
+  if (rc) return rc;
+  switch (epi) {
+    case EPI_F32: return launch_epi<EPI_F32>(bn, ta, tbm, g, stream);
+    case EPI_BF16: return launch_epi<EPI_BF16>(bn, ta, tbm, g, stream);
+    case EPI_QKV: return launch_epi<EPI_QKV>(bn, ta, tbm, g, stream);
+    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(bn, ta, tbm, g, stream);
+    case EPI_RESID: return launch_epi<EPI_RESID>(bn, ta, tbm, g, stream);
+    default: return TB_ERR_ARG;
+  }
+}
+
+size_t gemm_workspace_bytes(int M, int N, int bn, int splits) {
+  if (splits <= 1) return 0;
+  const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+  return tiles * splits * bn * BM * sizeof(float);
+}
+
+}  // namespace tb

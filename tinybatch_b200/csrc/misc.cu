@@ -1,0 +1,106 @@
+// Embedding gather (+ first-norm prologue) and greedy argmax.
+#include "common.cuh"
+#include "host.h"
+
+namespace tb {
+
+// One CTA per token row: h = emb[id] (fp32), hg = bf16(h * g), sq = sum h^2.
+__global__ void __launch_bounds__(128) embed_kernel(const int* ids, const __nv_bfloat16* emb,
+                                                    int ld_emb, int d, int vocab,
+                                                    const __nv_bfloat16* g, float* h, int ld_h,
+                                                    __nv_bfloat16* hg, int ld_hg, float* sq) {
+  __shared__ float red[4];
+  const int m = blockIdx.x;
+  int id = ids[m];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) set_status(ERR_BAD_INDEX);
+    id = 0;
+  }
+  const __nv_bfloat16* src = emb + (size_t)id * ld_emb;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+    float v[8], gw[8], o[8];
+    load_bf16x8(src + c, v);
+    load_bf16x8(g + c, gw);
+    float* hp = h + (size_t)m * ld_h + c;
+    *reinterpret_cast<float4*>(hp) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(hp + 4) = make_float4(v[4], v[5], v[6], v[7]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      ss += v[j] * v[j];
+      o[j] = v[j] * gw[j];
+    }
+    store_bf16x8(hg + (size_t)m * ld_hg + c, o);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) sq[m] = red[0] + red[1] + red[2] + red[3];
+}
+
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+// One CTA per row; ties go to the smallest index (torch.argmax semantics).
+__global__ void __launch_bounds__(512) argmax_kernel(const float* logits, int ld, int N, int* out) {
+  __shared__ float sv[16];
+  __shared__ int si[16];
+  const float* row = logits + (size_t)blockIdx.x * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  const bool vec = (ld % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) % 16 == 0);
+  if (vec) {
+    const int n4 = N / 4;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(row)[i];
+      better(bv, bi, v.x, 4 * i);
+      better(bv, bi, v.y, 4 * i + 1);
+      better(bv, bi, v.z, 4 * i + 2);
+      better(bv, bi, v.w, 4 * i + 3);
+    }
+    for (int i = 4 * n4 + threadIdx.x; i < N; i += blockDim.x) better(bv, bi, row[i], i);
+  } else {
+    for (int i = threadIdx.x; i < N; i += blockDim.x) better(bv, bi, row[i], i);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, v, i);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bv = sv[0];
+    bi = si[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
+    out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+int embed_launch(const int* ids, int M, const void* emb, int ld_emb, int d, int vocab,
+                 const void* g, float* h, int ld_h, void* hg, int ld_hg, float* sq,
+                 cudaStream_t st) {
+  if (M < 0 || d <= 0 || d % 8 || ld_emb % 8 || ld_h % 4 || ld_hg % 8) return arg_err("embed shapes");
+  if (M == 0) return TB_OK;
+  embed_kernel<<<M, 128, 0, st>>>(ids, (const __nv_bfloat16*)emb, ld_emb, d, vocab,
+                                  (const __nv_bfloat16*)g, h, ld_h, (__nv_bfloat16*)hg, ld_hg, sq);
+  return host_err(cudaGetLastError(), "embed launch");
+}
+
+int argmax_launch(const float* logits, int ld, int M, int N, int* out, cudaStream_t st) {
+  if (M < 0 || N <= 0 || ld < N) return arg_err("argmax shapes");
+  if (M == 0) return TB_OK;
+  argmax_kernel<<<M, 512, 0, st>>>(logits, ld, N, out);
+  return host_err(cudaGetLastError(), "argmax launch");
+}
+
+}  // namespace tb
