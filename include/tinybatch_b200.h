@@ -60,8 +60,10 @@ int tb_status(unsigned int* code_h, int clear);
  *     rms_norm(h) . w^T of src/tinybatch/model.py:65-69.
  *   bn: output tile width (64, 128 or 256); splits: split-K factor;
  *   ws/ws_bytes: split-K scratch of at least tb_gemm_scratch_bytes(M, N, bn,
- *     splits) bytes (arrival counters, then fp32 partial tiles); unused and
- *     may be NULL when splits == 1.
+ *     splits) bytes: a fixed 64 KiB region of per-tile arrival counters (zero
+ *     when first handed over, left zero by every call; so one arena can serve
+ *     every GEMM), then fp32 partial tiles.  Unused and may be NULL when
+ *     splits == 1.
  */
 size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits);
 

@@ -138,25 +138,64 @@ def _mlp(w, p, x):
     return torch.nn.functional.silu(gate) * up
 
 
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.bfloat16).to(torch.float32)
+
+
+def _normed_linear(h, g, wt, b, eps, emulate):
+    """``linear(rms_norm(h, g), wt, b)``.  With ``emulate`` the norm is
+    applied the way the GPU path does it: the GEMM reads bf16(h * g) and its
+    rows are scaled by rsqrt(mean(h^2) + eps) afterwards (same value in exact
+    arithmetic, bf16 rounding at the GEMM input)."""
+    if not emulate:
+        return linear(rms_norm(h, g, eps), wt, b)
+    h = _f32(h)
+    s = torch.rsqrt(h.square().mean(dim=-1, keepdim=True) + eps)
+    y = linear(_bf16(h * _f32(g)), wt) * s
+    return y if b is None else y + _f32(b)
+
+
 def paged_layer(cfg, w, layer: int, h, positions, seq_slices, block_tables, context_lens,
-                pool, block_size: int):
+                pool, block_size: int, emulate_bf16: bool = False):
     """One decoder layer of ``Qwen2Paged.forward`` (``src/tinybatch/model.py:114-154``):
     norm -> q/k/v (+bias) -> RoPE -> KV scatter -> per-sequence attention over
-    the paged context -> o_proj + residual -> norm -> SwiGLU MLP + residual."""
+    the paged context -> o_proj + residual -> norm -> SwiGLU MLP + residual.
+
+    ``emulate_bf16`` rounds to bf16 where the GPU path stores bf16 (GEMM
+    inputs, q, the KV pool, the attention output, the SwiGLU output) while
+    keeping every sum in fp32 -- a model of a correct bf16-storage forward
+    used to bound the kernels' own error."""
     p = f"model.layers.{layer}."
-    x = rms_norm(h, w[p + "input_layernorm.weight"], cfg.rms_eps)
-    q, k, v = _layer_qkv(cfg, w, p, x, cfg.n_heads, cfg.n_kv_heads)
-    q = rope(q, positions, cfg.rope_theta)
-    k = rope(k, positions, cfg.rope_theta)
+    T = h.shape[0]
+    g_in = w[p + "input_layernorm.weight"]
+    n_heads, n_kv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    q = _normed_linear(h, g_in, w[p + "self_attn.q_proj.weight"],
+                       w.get(p + "self_attn.q_proj.bias"), cfg.rms_eps, emulate_bf16)
+    k = _normed_linear(h, g_in, w[p + "self_attn.k_proj.weight"],
+                       w.get(p + "self_attn.k_proj.bias"), cfg.rms_eps, emulate_bf16)
+    v = _normed_linear(h, g_in, w[p + "self_attn.v_proj.weight"],
+                       w.get(p + "self_attn.v_proj.bias"), cfg.rms_eps, emulate_bf16)
+    q = rope(q.view(T, n_heads, hd), positions, cfg.rope_theta)
+    k = rope(k.view(T, n_kv, hd), positions, cfg.rope_theta)
+    v = v.view(T, n_kv, hd)
+    if emulate_bf16:
+        q, k, v = _bf16(q), _bf16(k), _bf16(v)
     kv_write(pool, k, v, positions, seq_slices, block_tables, block_size)
-    attn = torch.empty(h.shape[0], cfg.n_heads * cfg.head_dim)
+    attn = torch.empty(T, n_heads * hd)
     for (s, e), table, ctx in zip(seq_slices, block_tables, context_lens):
         keys, vals = kv_gather(pool, table, ctx)
         out = attention(q[s:e], keys, vals, first_pos=ctx - (e - s))
         attn[s:e] = out.reshape(e - s, -1)
+    if emulate_bf16:
+        attn = _bf16(attn)
     h = h + linear(attn, w[p + "self_attn.o_proj.weight"])
-    x = rms_norm(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
-    return h + linear(_mlp(w, p, x), w[p + "mlp.down_proj.weight"])
+    g_post = w[p + "post_attention_layernorm.weight"]
+    gate = _normed_linear(h, g_post, w[p + "mlp.gate_proj.weight"], None, cfg.rms_eps, emulate_bf16)
+    up = _normed_linear(h, g_post, w[p + "mlp.up_proj.weight"], None, cfg.rms_eps, emulate_bf16)
+    act = torch.nn.functional.silu(gate) * up
+    if emulate_bf16:
+        act = _bf16(act)
+    return h + linear(act, w[p + "mlp.down_proj.weight"])
 
 
 def embed(w, token_ids):
@@ -173,18 +212,19 @@ def lm_head_weight(cfg, w):
 
 @torch.inference_mode()
 def paged_forward(cfg, w, token_ids, positions, seq_slices, block_tables, context_lens,
-                  pools, block_size: int) -> torch.Tensor:
+                  pools, block_size: int, emulate_bf16: bool = False) -> torch.Tensor:
     """``Qwen2Paged.forward`` (``src/tinybatch/model.py:100-158``): logits of the
     last token of every sequence, ``[n_seqs, vocab]`` fp32.  ``pools`` are
-    updated in place, like the reference's ``PagedKVCache``."""
+    updated in place, like the reference's ``PagedKVCache``.  See
+    ``paged_layer`` for ``emulate_bf16``."""
     positions = torch.as_tensor(positions, dtype=torch.long)
     h = embed(w, token_ids)
     for layer in range(cfg.n_layers):
         h = paged_layer(cfg, w, layer, h, positions, seq_slices, block_tables, context_lens,
-                        pools[layer], block_size)
-    h = rms_norm(h, w["model.norm.weight"], cfg.rms_eps)
+                        pools[layer], block_size, emulate_bf16)
     last = torch.tensor([e - 1 for _, e in seq_slices], dtype=torch.long)
-    return linear(h[last], lm_head_weight(cfg, w))
+    return _normed_linear(h[last], w["model.norm.weight"], lm_head_weight(cfg, w), None,
+                          cfg.rms_eps, emulate_bf16)
 
 
 def shard(w: dict, rank: int, world: int) -> dict:

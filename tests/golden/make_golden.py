@@ -22,8 +22,9 @@ Cases:
                and logits are recorded
   bm_trace     random allocate/append/free sequence against BlockManager
   sched_trace  random admission/decode/finish sequence against Scheduler
-  qwen05b      config "qwen2.5-0.5b" (seed 1): two prompts, paged prefill
-               and one decode step; top-64 logits and a fixed index sample
+  qwen05b      config "qwen2.5-0.5b" (seed 1, bf16-valued weights): two
+               prompts, paged prefill and one decode step; top-64 logits
+               and a fixed index sample
 """
 from __future__ import annotations
 
@@ -258,7 +259,10 @@ def main() -> None:
     # ---- 0.5B-shaped probe
     if not args.skip_05b:
         cfg = named_config("qwen2.5-0.5b")
+        # config 2 specifies bf16 weights: the reference runs its fp32
+        # forward on the bf16-valued draw
         w = synthetic_weights(cfg, seed=1)
+        w = {k: v.to(torch.bfloat16).to(torch.float32) for k, v in w.items()}
         rng = random.Random(5)
         p0 = [rng.randrange(cfg.vocab_size) for _ in range(40)]
         p1 = [rng.randrange(cfg.vocab_size) for _ in range(17)]

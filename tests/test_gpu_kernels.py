@@ -249,3 +249,18 @@ def test_embed_and_argmax():
     torch.testing.assert_close(sq[0], ref_h.square().sum(1), rtol=1e-4, atol=1e-4)
     assert am.tolist() == logits.argmax(1).tolist()
     assert int(am[3]) == 17
+
+
+def test_split_k_calls_share_one_arena():
+    """Split-K GEMMs with different tile counts reuse one scratch arena: the
+    arrival counters must not alias an earlier call's partial tiles."""
+    arena = ops.Scratch(DEV, 1 << 20)
+    shapes = [(40, 256, 2048, 64, 8), (57, 4096, 896, 256, 3), (1, 152064 // 8, 896, 256, 3),
+              (40, 256, 2048, 64, 8)]
+    for i, (M, N, K, bn, splits) in enumerate(shapes):
+        x = _rand(M, K, seed=20 + i)
+        w = _rand(N, K, scale=1 / math.sqrt(K), seed=30 + i)
+        out = torch.empty(M, N, device=DEV)
+        ops.linear(x, w, out, bn=bn, splits=splits, scratch=arena)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out, x.float() @ w.float().t(), atol=2e-3, rtol=2e-3)

@@ -156,6 +156,7 @@ def test_qwen05b_probe_matches_reference(golden):
     case = golden["qwen05b"]
     cfg = named_config(case["cfg"])
     w = synthetic_weights(cfg, case["seed"])
+    w = {k: v.to(torch.bfloat16).to(torch.float32) for k, v in w.items()}
     assert float(w["model.embed_tokens.weight"].double().abs().sum()) == pytest.approx(
         case["fingerprint_embed"], rel=1e-12)
     p0, p1 = case["prompts"]

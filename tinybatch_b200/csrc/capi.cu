@@ -19,6 +19,13 @@ namespace {
 constexpr size_t ALIGN = 256;
 inline size_t round_up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
 
+// Split-K scratch layout: a fixed region of per-tile arrival counters (kept
+// at zero between calls) followed by the fp32 partial tiles.  The counter
+// region never moves, so calls with different tile counts can share one
+// arena without reading another call's partials as counters.
+constexpr size_t COUNTER_TILES = 16384;
+constexpr size_t COUNTER_BYTES = COUNTER_TILES * sizeof(int);
+
 size_t tiles_of(int M, int N, int bn) {
   return (size_t)((M + 127) / 128) * (size_t)((N + bn - 1) / bn);
 }
@@ -29,11 +36,12 @@ int gemm_scratch(GemmArgs& g, int bn, void* ws, size_t ws_bytes) {
   g.counters = nullptr;
   if (g.splits <= 1) return TB_OK;
   const size_t tiles = tiles_of(g.M, g.N, bn);
-  const size_t need = round_up(tiles * sizeof(int)) + tiles * g.splits * bn * 128 * sizeof(float);
+  if (tiles > COUNTER_TILES) return arg_err("split-K over more than 16384 tiles");
+  const size_t need = COUNTER_BYTES + tiles * g.splits * bn * 128 * sizeof(float);
   if (ws == nullptr || ws_bytes < need) return arg_err("split-K scratch too small");
   if (reinterpret_cast<uintptr_t>(ws) % ALIGN) return arg_err("scratch must be 256-byte aligned");
   g.counters = static_cast<int*>(ws);
-  g.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + round_up(tiles * sizeof(int)));
+  g.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + COUNTER_BYTES);
   return TB_OK;
 }
 
@@ -76,7 +84,7 @@ int tb_status(unsigned int* code_h, int clear) {
 size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits) {
   if (splits <= 1) return 0;
   const size_t tiles = tiles_of(M, N, bn);
-  return round_up(tiles * sizeof(int)) + tiles * splits * bn * 128 * sizeof(float);
+  return COUNTER_BYTES + tiles * splits * bn * 128 * sizeof(float);
 }
 
 int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,

@@ -1,0 +1,363 @@
+"""Device-side forward of the (tensor-parallel) paged Qwen2 model on one rank.
+
+Per decoder layer the forward is five kernel launches, all from the C ABI:
+
+  1. tb_qkv_rope_kv          column-parallel q|k|v GEMM; epilogue applies the
+                             deferred input RMSNorm, bias and RoPE, writes q
+                             and scatters k, v into the paged pool
+  2. tb_paged_attention_*    GQA attention over the pool through block tables
+  3. tb_row_linear_residual  row-parallel o_proj; epilogue: (all-reduce,)
+                             residual add, next-norm prologue (h*g, sum h^2)
+  4. tb_gate_up_swiglu       column-parallel gate|up GEMM with SwiGLU epilogue
+  5. tb_row_linear_residual  row-parallel down_proj, same epilogue as 3
+
+The residual stream ``h`` stays fp32 on the device.  RMSNorm is never a
+separate pass: the row-parallel epilogue stores ``hg = bf16(h * g)`` and
+per-tile partial sums of ``h^2``; the next GEMM multiplies its rows by
+``rsqrt(mean(h^2) + eps)``, which equals ``rms_norm(h, g) @ W^T``
+(``src/tinybatch/model.py:65-69``).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import ops
+from .config import ModelConfig
+
+SMS = 148
+
+
+# ------------------------------------------------------------------ planning
+
+def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 256), max_splits: int = 16) -> tuple[int, int]:
+    """Tile width and split-K factor for a C[M,N] = A[M,K] B[N,K]^T launch.
+
+    Cost model (arbitrary units): a CTA streams (bn + 32) * k_iters bf16 rows
+    of 64 (B tile plus the share of the A tile that misses L2), pays a fixed
+    setup cost, and a split pays its fp32 partial round trip; the launch
+    takes ceil(CTAs / 148) such waves."""
+    tm = -(-M // 128)
+    num_k = -(-K // 64)
+    best = None
+    for bn in bns:
+        tiles = tm * -(-N // bn)
+        for s in range(1, max_splits + 1):
+            if s > num_k or (s > 1 and num_k / s < 4):
+                break
+            ctas = tiles * s
+            waves = -(-ctas // SMS)
+            per_cta = -(-num_k // s) * (bn + 32) + 160 + (bn if s > 1 else 0)
+            cost = waves * per_cta
+            if best is None or cost < best[0]:
+                best = (cost, bn, s)
+    return best[1], best[2]
+
+
+# ------------------------------------------------------------------ weights
+
+@dataclass
+class LayerWeights:
+    wqkv: torch.Tensor   # [(Hq+2Hkv)/t*hd, d]
+    bqkv: torch.Tensor   # [(Hq+2Hkv)/t*hd]
+    wo: torch.Tensor     # [d, Hq/t*hd]
+    wgu: torch.Tensor    # [tiles*gu_bn, d] interleaved gate/up
+    wd: torch.Tensor     # [d, ff/t]
+    ln_in: torch.Tensor  # [d]
+    ln_post: torch.Tensor
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, bn: int) -> torch.Tensor:
+    """Rows of tile t: gate rows of features [t*bn/2, (t+1)*bn/2), then the
+    matching up rows; the last tile is padded with zero rows."""
+    F, K = gate.shape
+    half = bn // 2
+    tiles = -(-F // half)
+    out = torch.zeros(tiles, 2, half, K, dtype=gate.dtype, device=gate.device)
+    pad = tiles * half - F
+    g = torch.nn.functional.pad(gate, (0, 0, 0, pad)).view(tiles, half, K)
+    u = torch.nn.functional.pad(up, (0, 0, 0, pad)).view(tiles, half, K)
+    out[:, 0] = g
+    out[:, 1] = u
+    return out.view(tiles * bn, K)
+
+
+class RankWeights:
+    """One tensor-parallel rank's weights, packed for the fused kernels, bf16
+    on the rank's device.  ``w`` is the full (unsharded) HF-named dict; the
+    split is the Megatron one of ``src/tinybatch/tensor_parallel.py:35-61``."""
+
+    GU_BN = 128
+
+    def __init__(self, cfg: ModelConfig, w: dict, rank: int = 0, world: int = 1,
+                 device="cuda", sharded: bool = False):
+        assert cfg.n_heads % world == 0, "q heads must divide tp degree"
+        assert cfg.n_kv_heads % world == 0, "kv heads must divide tp degree"
+        assert cfg.d_ff % world == 0, "d_ff must divide tp degree"
+        self.cfg, self.rank, self.world = cfg, rank, world
+        self.device = torch.device(device)
+        bf = torch.bfloat16
+
+        def dev(t):
+            return t.detach().to(device=self.device, dtype=bf).contiguous()
+
+        def col(t):
+            return dev(t if sharded else t.chunk(world, dim=0)[rank])
+
+        def row(t):
+            return dev(t if sharded else t.chunk(world, dim=1)[rank])
+
+        self.n_q = cfg.n_heads // world
+        self.n_kv = cfg.n_kv_heads // world
+        self.ff = cfg.d_ff // world
+        self.layers: list[LayerWeights] = []
+        for i in range(cfg.n_layers):
+            p = f"model.layers.{i}."
+            q, k, v = (col(w[p + f"self_attn.{n}_proj.weight"]) for n in "qkv")
+            biases = []
+            for n, rows in (("q", q.shape[0]), ("k", k.shape[0]), ("v", v.shape[0])):
+                b = w.get(p + f"self_attn.{n}_proj.bias")
+                biases.append(col(b) if b is not None else torch.zeros(rows, dtype=bf, device=self.device))
+            self.layers.append(LayerWeights(
+                wqkv=torch.cat([q, k, v], 0).contiguous(),
+                bqkv=torch.cat(biases, 0).contiguous(),
+                wo=row(w[p + "self_attn.o_proj.weight"]),
+                wgu=interleave_gate_up(col(w[p + "mlp.gate_proj.weight"]),
+                                       col(w[p + "mlp.up_proj.weight"]), self.GU_BN).contiguous(),
+                wd=row(w[p + "mlp.down_proj.weight"]),
+                ln_in=dev(w[p + "input_layernorm.weight"]),
+                ln_post=dev(w[p + "post_attention_layernorm.weight"]),
+            ))
+        self.emb = dev(w["model.embed_tokens.weight"])
+        head = w.get("lm_head.weight")
+        tied = head is None or head is w["model.embed_tokens.weight"]
+        self.lm_head = self.emb if tied else dev(head)
+        self.final_norm = dev(w["model.norm.weight"])
+        self.rope_cos, self.rope_sin = rope_tables(cfg, self.device)
+
+
+def rope_tables(cfg: ModelConfig, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 cos/sin [max_position, hd/2] with the reference's arithmetic
+    (``src/tinybatch/model.py:75-77``: inv_freq = 1/theta^(arange(0,hd,2)/hd),
+    angle = float(pos) * inv_freq), computed once on the CPU."""
+    hd = cfg.head_dim
+    inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
+    ang = torch.arange(cfg.max_position, dtype=torch.float32)[:, None] * inv_freq[None, :]
+    return ang.cos().to(device).contiguous(), ang.sin().to(device).contiguous()
+
+
+# ------------------------------------------------------------------ metadata
+
+class StepMeta:
+    """Device int32 metadata of one flat mixed batch, built on the host with
+    numpy and shipped in one host->device copy.
+
+    Fields: ids, positions, slots [T]; row_dst [T] (sequence index of each
+    sequence's last token, else -1); for the decode subset (q_len*G <= 16)
+    and the prefill subset: q_start, q_len, ctx_len [n], block tables
+    [n, bt_ld] (-1 padded); the prefill (sequence, 64-row tile) work list."""
+
+    def __init__(self, token_ids, positions, seq_slices, block_tables, context_lens,
+                 block_size: int, group: int, device, pinned: bool = True,
+                 all_logits: bool = False):
+        if isinstance(token_ids, torch.Tensor):
+            token_ids = token_ids.detach().cpu().numpy()
+        if isinstance(positions, torch.Tensor):
+            positions = positions.detach().cpu().numpy()
+        ids = np.asarray(token_ids, dtype=np.int64).astype(np.int32)
+        pos = np.asarray(positions, dtype=np.int64).astype(np.int32)
+        T = ids.shape[0]
+        n = len(seq_slices)
+        starts = np.fromiter((s for s, _ in seq_slices), dtype=np.int32, count=n)
+        ends = np.fromiter((e for _, e in seq_slices), dtype=np.int32, count=n)
+        qlen = ends - starts
+        ctx = np.asarray(context_lens, dtype=np.int32)
+        # slot of every token: table[p // bs] * bs + p % bs
+        slots = np.empty(T, dtype=np.int32)
+        for i, ((s, e), table) in enumerate(zip(seq_slices, block_tables)):
+            if e > s:
+                tbl = np.asarray(table, dtype=np.int64)
+                p = pos[s:e].astype(np.int64)
+                slots[s:e] = (tbl[p // block_size] * block_size + p % block_size).astype(np.int32)
+        if all_logits:          # every token row gets logits (tp_forward)
+            row_dst = np.arange(T, dtype=np.int32)
+        else:
+            row_dst = np.full(T, -1, dtype=np.int32)
+            row_dst[ends[qlen > 0] - 1] = np.nonzero(qlen > 0)[0].astype(np.int32)
+        self.n_out = T if all_logits else n
+        is_dec = qlen * group <= 16
+        self.T, self.n = T, n
+        self.group = group
+
+        def subset(mask):
+            idx = np.nonzero(mask)[0]
+            bt_ld = max([len(block_tables[i]) for i in idx], default=1) or 1
+            bt = np.full((len(idx), bt_ld), -1, dtype=np.int32)
+            for r, i in enumerate(idx):
+                bt[r, :len(block_tables[i])] = block_tables[i]
+            return idx, starts[idx], qlen[idx], ctx[idx], bt
+
+        d_idx, d_qs, d_ql, d_ctx, d_bt = subset(is_dec)
+        p_idx, p_qs, p_ql, p_ctx, p_bt = subset(~is_dec)
+        work = [(r, t) for r, ql in enumerate(p_ql) for t in range(-(-int(ql) * group // 64))]
+        work = np.asarray(work, dtype=np.int32).reshape(-1, 2)
+        parts = [ids, pos, slots, row_dst, d_qs, d_ql, d_ctx, d_bt.ravel(), p_qs, p_ql, p_ctx,
+                 p_bt.ravel(), work.ravel()]
+        flat = np.concatenate(parts).astype(np.int32)
+        host = torch.from_numpy(flat)
+        if pinned and torch.device(device).type == "cuda":
+            host = host.pin_memory()
+        buf = host.to(device, non_blocking=True)
+        self.h2d_bytes = flat.nbytes
+        views, o = [], 0
+        for a in parts:
+            views.append(buf[o:o + a.size])
+            o += a.size
+        (self.ids, self.positions, self.slots, self.row_dst, self.dec_q_start, self.dec_q_len,
+         self.dec_ctx, dbt, self.pre_q_start, self.pre_q_len, self.pre_ctx, pbt, wk) = views
+        self.dec_bt = dbt.view(len(d_idx), d_bt.shape[1])
+        self.pre_bt = pbt.view(len(p_idx), p_bt.shape[1])
+        self.work = wk.view(-1, 2)
+        self.n_dec, self.n_pre = len(d_idx), len(p_idx)
+        self.dec_ctx_sum = int(d_ctx.astype(np.int64).sum())
+        self.pre_ctx_sum = int(p_ctx.astype(np.int64).sum())
+        self.dec_tokens = int(d_ql.astype(np.int64).sum())
+        # causal (query, key) pairs of the prefill subset, for the flop count
+        first = (p_ctx - p_ql).astype(np.int64)
+        ql = p_ql.astype(np.int64)
+        self.pre_pairs = int((ql * first + ql * (ql + 1) // 2).sum())
+        self.dec_max_ctx = int(d_ctx.max()) if len(d_idx) else 1
+        self._keep = (host, buf)
+
+
+# ------------------------------------------------------------------ forward
+
+class DeviceModel:
+    """Buffers and the launch sequence of the forward on one rank."""
+
+    def __init__(self, weights: RankWeights, max_tokens: int = 2048, max_seqs: int = 256,
+                 comm=None, split_tokens: int = 512):
+        self.w = weights
+        self.cfg = weights.cfg
+        self.device = weights.device
+        self.comm = comm
+        self.split_tokens = split_tokens
+        # split-K scratch (arrival counters must stay zero between calls) and
+        # split-KV attention scratch live in separate arenas
+        self.scratch = ops.Scratch(self.device, 1 << 20)
+        self.attn_scratch = ops.Scratch(self.device, 1 << 20)
+        # when a list, every launch appends (kind, start event, end event,
+        # algorithmic bytes, flops) -- used by the benchmark's roofline
+        self.prof: list | None = None
+        self._alloc(max_tokens, max_seqs)
+
+    def _run(self, kind: str, nbytes: float, flops: float, fn, *a, **kw):
+        if self.prof is None:
+            return fn(*a, **kw)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        r = fn(*a, **kw)
+        e.record()
+        self.prof.append((kind, s, e, nbytes, flops))
+        return r
+
+    def _alloc(self, T: int, S: int) -> None:
+        cfg, w, dev = self.cfg, self.w, self.device
+        d = cfg.d_model
+        self.T_max, self.S_max = T, S
+        self.parts_max = max(-(-d // 64), 1)
+        self.h = torch.zeros(T, d, device=dev)
+        self.hg = torch.zeros(T, d, device=dev, dtype=torch.bfloat16)
+        self.sq = torch.zeros(self.parts_max, T, device=dev)
+        self.q = torch.zeros(T, w.n_q * cfg.head_dim, device=dev, dtype=torch.bfloat16)
+        self.attn = torch.zeros(T, w.n_q * cfg.head_dim, device=dev, dtype=torch.bfloat16)
+        ff_pad = -(-w.ff // 64) * 64
+        self.act = torch.zeros(T, ff_pad, device=dev, dtype=torch.bfloat16)
+        self.hg_last = torch.zeros(S, d, device=dev, dtype=torch.bfloat16)
+        self.sq_last = torch.zeros(self.parts_max, S, device=dev)
+        v_pad = -(-cfg.vocab_size // 4) * 4      # fp32 rows stay 16-byte aligned
+        self.logits = torch.zeros(S, v_pad, device=dev)[:, :cfg.vocab_size]
+        self.next_ids = torch.zeros(S, dtype=torch.int32, device=dev)
+
+    def ensure(self, T: int, S: int) -> None:
+        if T > self.T_max or S > self.S_max:
+            self._alloc(max(T, self.T_max), max(S, self.S_max))
+
+    # one row-parallel projection: residual (+ all-reduce) + norm prologue
+    def _row(self, x, wmat, g_next, T, last: bool, md: StepMeta):
+        bn, splits = plan_gemm(T, wmat.shape[0], wmat.shape[1])
+        kw = dict(bn=bn, splits=splits, scratch=self.scratch)
+        if last:
+            kw.update(row_dst=md.row_dst, hg2=self.hg_last, sq2=self.sq_last)
+        Nn, K = wmat.shape
+        nbytes = 2 * Nn * K + 2 * T * K + T * Nn * (4 + 4 + 2)
+        fn = ops.row_linear_residual if self.comm is None else self.comm.row_linear_residual
+        self._run("row_gemm_residual", nbytes, 2.0 * T * Nn * K, fn, x, wmat, self.h[:T], g_next,
+                  self.hg[:T], self.sq, **kw)
+        return -(-Nn // bn)
+
+    def forward(self, md: StepMeta, kv_pools: list[torch.Tensor], compute_logits: bool = True,
+                sample: bool = False):
+        cfg, W = self.cfg, self.w
+        T, n = md.T, md.n_out
+        self.ensure(T, n)
+        d, hd = cfg.d_model, cfg.head_dim
+        inv_d, eps = 1.0 / d, cfg.rms_eps
+        bs = kv_pools[0].shape[3]
+        self._run("embed", T * d * (2 + 4 + 2), 0.0, ops.embed, md.ids, W.emb, W.layers[0].ln_in,
+                  self.h[:T], self.hg[:T], self.sq[0])
+        kv_row = 2 * W.n_kv * hd * 2          # K+V bytes of one token in one layer
+        dec_ctx = md.dec_ctx_sum
+        pre_ctx = md.pre_ctx_sum
+        parts = 1
+        for li, L in enumerate(W.layers):
+            pool = kv_pools[li]
+            bn, splits = plan_gemm(T, L.wqkv.shape[0], d, bns=(128, 256) if hd > 64 else (64, 128, 256))
+            Nq = L.wqkv.shape[0]
+            self._run("qkv_rope_kv", 2 * Nq * d + 2 * T * d + 2 * T * Nq, 2.0 * T * Nq * d,
+                      ops.qkv_rope_kv, self.hg[:T], L.wqkv, L.bqkv, n_q_heads=W.n_q, n_kv_heads=W.n_kv,
+                            head_dim=hd, sq=self.sq[:parts], inv_d=inv_d, eps=eps,
+                            rope_cos=W.rope_cos, rope_sin=W.rope_sin, positions=md.positions,
+                            slots=md.slots, q_out=self.q[:T], kv_pool=pool, block_size=bs,
+                            bn=bn, splits=splits, scratch=self.scratch)
+            akw = dict(n_q_heads=W.n_q, n_kv_heads=W.n_kv, head_dim=hd, block_size=bs)
+            qrow = W.n_q * hd * 2
+            if md.n_dec:
+                self._run(
+                    "attention_decode", dec_ctx * kv_row + 2 * md.dec_tokens * qrow,
+                    4.0 * md.dec_ctx_sum * W.n_q * hd, ops.paged_attention_decode,
+                    self.q, self.attn, pool, block_tables=md.dec_bt, q_start=md.dec_q_start,
+                    q_len=md.dec_q_len, ctx_len=md.dec_ctx, max_ctx=md.dec_max_ctx,
+                    split_tokens=self.split_tokens, scratch=self.attn_scratch, **akw)
+            if md.n_pre:
+                self._run(
+                    "attention_prefill", pre_ctx * kv_row + 2 * (T - md.dec_tokens) * qrow,
+                    4.0 * md.pre_pairs * W.n_q * hd, ops.paged_attention_prefill,
+                    self.q, self.attn, pool, block_tables=md.pre_bt, q_start=md.pre_q_start,
+                    q_len=md.pre_q_len, ctx_len=md.pre_ctx, work=md.work, **akw)
+            parts = self._row(self.attn[:T], L.wo, L.ln_post, T, False, md)
+            bn = RankWeights.GU_BN
+            _, splits = plan_gemm(T, L.wgu.shape[0], d, bns=(bn,))
+            Ngu = L.wgu.shape[0]
+            self._run("gate_up_swiglu", 2 * Ngu * d + 2 * T * d + 2 * T * W.ff, 2.0 * T * Ngu * d,
+                      ops.gate_up_swiglu, self.hg[:T], L.wgu, self.act[:T], n_feat=W.ff,
+                      sq=self.sq[:parts], inv_d=inv_d, eps=eps, bn=bn, splits=splits,
+                      scratch=self.scratch)
+            last = li == len(W.layers) - 1
+            g_next = W.final_norm if last else W.layers[li + 1].ln_in
+            parts = self._row(self.act[:T, :W.ff], L.wd, g_next, T, last, md)
+        if not compute_logits:
+            return None
+        bn, splits = plan_gemm(n, cfg.vocab_size, d)
+        out = self.logits[:n]
+        V = cfg.vocab_size
+        self._run("lm_head", 2 * V * d + 2 * n * d + 4 * n * V, 2.0 * n * V * d, ops.linear,
+                  self.hg_last[:n], W.lm_head, out, sq=self.sq_last[:parts], inv_d=inv_d,
+                  eps=eps, bn=bn, splits=splits, scratch=self.scratch)
+        if sample:
+            self._run("argmax", 4 * n * V, 0.0, ops.argmax, out, self.next_ids[:n])
+        return out
