@@ -75,6 +75,33 @@ int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int 
               void* out, int ld_out, int out_f32, int bn, int splits,
               void* ws, size_t ws_bytes, void* stream);
 
+/* Bytes of split-K scratch built into the library for
+ * tb_linear_static_scratch: 4 KiB of arrival counters (at most 1024 output
+ * tiles) followed by fp32 partial tiles. */
+#define TB_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* tb_linear for callers that cannot allocate device memory (no counterpart
+ * in the reference).  Some callers may not call cudaMalloc at all -- code
+ * running inside a custom allocator, or next to a framework that has already
+ * reserved all device memory for its own pool -- yet still want the split-K
+ * projection, which needs scratch for its partial tiles.  This variant takes
+ * that scratch from a fixed array inside the library
+ * (TB_STATIC_SCRATCH_BYTES per device, held by every GPU that loads the
+ * library until the process exits) and allocates nothing.  Arguments and
+ * result are those of tb_linear without ws/ws_bytes.
+ *   - A call whose split-K scratch would exceed the array (or 1024 tiles)
+ *     fails with TB_ERR_ARG and a message naming the size it needed.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - All calls on a device share the array and it keeps the last call's
+ *     contents; each call clears the counters it needs.  Calls that may run
+ *     at the same time on one device (unordered streams) race on it. */
+int tb_linear_static_scratch(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
+                             const float* sq, int sq_parts, int sq_ld, float inv_d, float eps,
+                             void* out, int ld_out, int out_f32, int bn, int splits,
+                             void* stream);
+
 /* Column-parallel fused QKV projection.  w_qkv = [Wq; Wk; Wv] of this rank's
  * heads ([(Hq+2Hkv)*hd, K]), bias likewise.  Epilogue: rowscale, + bias,
  * NeoX RoPE of q and k with the fp32 tables rope_cos/rope_sin

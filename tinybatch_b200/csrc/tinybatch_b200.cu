@@ -5,3 +5,4 @@
 #include "attention.cu"
 #include "misc.cu"
 #include "capi.cu"
+#include "static_scratch.cu"
