@@ -58,14 +58,24 @@ int tb_status(unsigned int* code_h, int clear);
  *     rsqrt(inv_d * sum_{p<sq_parts} sq[p*sq_ld + m] + eps), i.e. x holds
  *     h * norm_weight and sq holds partial sums of h^2 — exactly
  *     rms_norm(h) . w^T of src/tinybatch/model.py:65-69.
- *   bn: output tile width (64, 128 or 256); splits: split-K factor;
- *   ws/ws_bytes: split-K scratch of at least tb_gemm_scratch_bytes(M, N, bn,
- *     splits) bytes: a fixed 64 KiB region of per-tile arrival counters (zero
- *     when first handed over, left zero by every call; so one arena can serve
- *     every GEMM), then fp32 partial tiles.  Unused and may be NULL when
- *     splits == 1.
+ *   bn: output tile width (64, 128, 192 or 256); splits: split-K factor.
+ *   ws/ws_bytes: how split-K partials are combined.
+ *     ws == NULL, splits in 2..8: the splits of an output tile run as one
+ *       thread-block cluster; each CTA parks its fp32 partial in its shared
+ *       memory and reduces a slice of the tile's columns over distributed
+ *       shared memory, in split order (deterministic, no scratch).
+ *     ws != NULL: partials go through caller scratch of at least
+ *       tb_gemm_scratch_bytes(M, N, bn, splits) bytes: a fixed 64 KiB region
+ *       of per-tile arrival counters (zero when first handed over, left zero
+ *       by every call, so one arena can serve every GEMM), then fp32 partial
+ *       tiles; the last CTA of a tile to arrive reduces them.
+ *     Unused when splits == 1.
  */
 size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits);
+
+/* How many clusters of `cluster` GEMM CTAs (tile width bn) fit on the current
+ * device at once (cudaOccupancyMaxActiveClusters); for choosing splits. */
+int tb_gemm_max_active_clusters(int bn, int cluster, int* out_h);
 
 /* Plain projection: out = rowscale * x . w^T, fp32 (out_f32=1) or bf16.
  * Replaces F.linear of the LM head (src/tinybatch/model.py:158,

@@ -44,19 +44,25 @@ GEMM_CASES = [
     (77, 97, 64, 64, 1),
     (128, 64, 32, 64, 1),
     (300, 512, 1024, 256, 1),
+    (128, 576, 1024, 192, 1),
     (128, 512, 1024, 128, 2),
     (64, 640, 1344, 128, 3),
     (130, 256, 4096, 256, 5),
+    (128, 960, 2048, 192, 4),
+    (100, 384, 4096, 64, 8),
 ]
 
 
+@pytest.mark.parametrize("split_mode", ["cluster", "global"])
 @pytest.mark.parametrize("M,N,K,bn,splits", GEMM_CASES)
-def test_linear_f32(M, N, K, bn, splits):
+def test_linear_f32(M, N, K, bn, splits, split_mode):
+    if splits == 1 and split_mode == "global":
+        pytest.skip("no split")
     x = _rand(M, K, seed=1)
     w = _rand(N, K, scale=1 / math.sqrt(K), seed=2)
     ld = (N + 3) // 4 * 4
     out = torch.full((M, ld), float("nan"), device=DEV)
-    ops.linear(x, w, out, bn=bn, splits=splits)
+    ops.linear(x, w, out, bn=bn, splits=splits, split_mode=split_mode)
     torch.cuda.synchronize()
     ref = x.float() @ w.float().t()
     torch.testing.assert_close(out[:, :N], ref, atol=2e-3, rtol=2e-3)
@@ -75,9 +81,11 @@ def test_linear_rowscale_bf16():
     torch.testing.assert_close(out.float(), ref, atol=1.6e-2, rtol=1.6e-2)
 
 
-@pytest.mark.parametrize("M,N,K,bn,splits", [(128, 512, 640, 128, 1), (37, 256, 1024, 64, 4),
-                                             (260, 896, 896, 128, 1)])
-def test_row_linear_residual(M, N, K, bn, splits):
+@pytest.mark.parametrize("M,N,K,bn,splits,mode", [
+    (128, 512, 640, 128, 1, "cluster"), (37, 256, 1024, 64, 4, "global"),
+    (37, 256, 1024, 64, 4, "cluster"), (260, 896, 896, 128, 1, "cluster"),
+    (128, 5120, 5120, 256, 7, "cluster"), (96, 896, 896, 192, 3, "cluster")])
+def test_row_linear_residual(M, N, K, bn, splits, mode):
     x = _rand(M, K, seed=5)
     w = _rand(N, K, scale=1 / math.sqrt(K), seed=6)
     h0 = torch.randn(M, N, device=DEV)
@@ -92,7 +100,7 @@ def test_row_linear_residual(M, N, K, bn, splits):
     hg2 = torch.zeros(2, N, dtype=torch.bfloat16, device=DEV)
     sq2 = torch.zeros(parts, 2, device=DEV)
     ops.row_linear_residual(x, w, h, g, hg, sq, row_dst=row_dst, hg2=hg2, sq2=sq2, bn=bn,
-                            splits=splits)
+                            splits=splits, split_mode=mode)
     torch.cuda.synchronize()
     href = h0 + x.float() @ w.float().t()
     torch.testing.assert_close(h, href, atol=2e-3, rtol=2e-3)
@@ -103,9 +111,11 @@ def test_row_linear_residual(M, N, K, bn, splits):
     torch.testing.assert_close(sq2[:, 0], sq[:, M - 1])
 
 
-@pytest.mark.parametrize("M,F,K,bn,splits", [(128, 256, 512, 128, 1), (50, 192, 896, 128, 2),
-                                             (200, 128, 256, 256, 1)])
-def test_gate_up_swiglu(M, F, K, bn, splits):
+@pytest.mark.parametrize("M,F,K,bn,splits,mode", [
+    (128, 256, 512, 128, 1, "cluster"), (50, 192, 896, 128, 2, "global"),
+    (50, 192, 896, 128, 2, "cluster"), (200, 128, 256, 256, 1, "cluster"),
+    (128, 1728, 640, 192, 2, "cluster"), (128, 864, 1024, 192, 1, "cluster")])
+def test_gate_up_swiglu(M, F, K, bn, splits, mode):
     x = _rand(M, K, seed=8)
     wg = _rand(F, K, scale=1 / math.sqrt(K), seed=9)
     wu = _rand(F, K, scale=1 / math.sqrt(K), seed=10)
@@ -118,7 +128,8 @@ def test_gate_up_swiglu(M, F, K, bn, splits):
         wgu[t * bn + half: t * bn + half + f1 - f0] = wu[f0:f1]
     sq = torch.rand(1, M, device=DEV) * K + 1
     act = torch.empty(M, F, dtype=torch.bfloat16, device=DEV)
-    ops.gate_up_swiglu(x, wgu, act, n_feat=F, sq=sq, inv_d=1 / K, eps=1e-6, bn=bn, splits=splits)
+    ops.gate_up_swiglu(x, wgu, act, n_feat=F, sq=sq, inv_d=1 / K, eps=1e-6, bn=bn, splits=splits,
+                       split_mode=mode)
     torch.cuda.synchronize()
     s = torch.rsqrt(sq[0] / K + 1e-6)[:, None]
     gate = (x.float() @ wg.float().t()) * s
@@ -127,9 +138,11 @@ def test_gate_up_swiglu(M, F, K, bn, splits):
     torch.testing.assert_close(act.float(), ref, atol=1.6e-2, rtol=1.6e-2)
 
 
-@pytest.mark.parametrize("hq,hkv,hd,bn,bs", [(4, 2, 16, 64, 16), (14, 2, 64, 128, 16),
-                                             (40, 8, 128, 128, 16), (5, 1, 128, 256, 4)])
-def test_qkv_rope_kv(hq, hkv, hd, bn, bs):
+@pytest.mark.parametrize("hq,hkv,hd,bn,bs,splits", [
+    (4, 2, 16, 64, 16, 1), (14, 2, 64, 128, 16, 1), (40, 8, 128, 128, 16, 1),
+    (5, 1, 128, 256, 4, 1), (40, 8, 128, 256, 16, 4), (14, 2, 64, 192, 16, 2),
+    (5, 1, 128, 128, 16, 3)])
+def test_qkv_rope_kv(hq, hkv, hd, bn, bs, splits):
     M, K = 70, 256
     N = (hq + 2 * hkv) * hd
     x = _rand(M, K, seed=11)
@@ -148,7 +161,8 @@ def test_qkv_rope_kv(hq, hkv, hd, bn, bs):
     sq = torch.rand(2, M, device=DEV) * K + 1
     ops.qkv_rope_kv(x, w, bias, n_q_heads=hq, n_kv_heads=hkv, head_dim=hd, sq=sq, inv_d=1 / K,
                     eps=1e-6, rope_cos=cos, rope_sin=sin, positions=pos.to(torch.int32).to(DEV),
-                    slots=slots.to(DEV), q_out=q, kv_pool=pool, block_size=bs, bn=bn)
+                    slots=slots.to(DEV), q_out=q, kv_pool=pool, block_size=bs, bn=bn,
+                    splits=splits)
     torch.cuda.synchronize()
     s = torch.rsqrt(sq.sum(0) / K + 1e-6)[:, None].cpu()
     y = (x.float().cpu() @ w.float().cpu().t()) * s + bias.float().cpu()
@@ -261,6 +275,12 @@ def test_split_k_calls_share_one_arena():
         x = _rand(M, K, seed=20 + i)
         w = _rand(N, K, scale=1 / math.sqrt(K), seed=30 + i)
         out = torch.empty(M, N, device=DEV)
-        ops.linear(x, w, out, bn=bn, splits=splits, scratch=arena)
+        ops.linear(x, w, out, bn=bn, splits=splits, scratch=arena, split_mode="global")
         torch.cuda.synchronize()
         torch.testing.assert_close(out, x.float() @ w.float().t(), atol=2e-3, rtol=2e-3)
+
+
+def test_cluster_occupancy_query():
+    for bn in (64, 128, 192, 256):
+        for c in (1, 2, 4, 8):
+            assert ops.max_active_clusters(bn, c) >= 1

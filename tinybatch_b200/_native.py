@@ -25,6 +25,7 @@ _SIGS = {
     "tb_last_error": (ctypes.c_char_p, []),
     "tb_status": (c_int, [ctypes.POINTER(c_uint), c_int]),
     "tb_gemm_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "tb_gemm_max_active_clusters": (c_int, [c_int, c_int, ctypes.POINTER(c_int)]),
     "tb_linear": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                           c_void_p, c_int, c_int, c_float, c_float,
                           c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),

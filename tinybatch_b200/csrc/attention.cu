@@ -14,11 +14,14 @@
 // cp.async (16-byte pieces, XOR-swizzled so ldmatrix is conflict-free);
 // softmax is the online (running max / running sum) form in base 2.
 //
-//   decode kernel   q_len*G <= 16 rows; one CTA per (split, kv head, seq);
-//                   the 4 warps take interleaved key chunks of the split and
+//   decode kernels  q_len*G <= 16 rows; one CTA per (split, kv head, seq);
+//                   4 warps take interleaved key chunks of the split and
 //                   merge their (max, sum, O) in shared memory; with more
 //                   than one split the CTA writes (O/l, log2 l + max) and
-//                   attn_combine_kernel merges the splits.
+//                   attn_combine_kernel merges the splits.  Chunks arrive by
+//                   TMA (a producer warp, 8-slot mbarrier ring) when the
+//                   block size is a multiple of 16 and hd is 64 or 128,
+//                   else by per-lane cp.async.
 //   prefill kernel  64 rows per CTA (16 per warp), key chunks shared by the
 //                   4 warps, causal limit per row.
 #include "attention.cuh"
@@ -97,8 +100,20 @@ __device__ __forceinline__ void load_chunk(const AttnArgs& a, const int* table, 
   }
 }
 
-// Per-warp flash state for 16 rows: thread holds rows lane/4 and lane/4+8.
+// 16-token chunk written by TMA with 128-byte swizzling: the head dimension
+// is cut in 64-element halves, each a [16 rows][128 B] box whose 16-byte units
+// are XOR-permuted by (row % 8); halves are 2 KiB apart.
 template <int HD>
+struct TmaChunkLayout {
+  static constexpr int BYTES = 16 * HD * 2;
+  __device__ static __forceinline__ int off(int t, int c) {
+    return (c >> 3) * 2048 + t * 128 + (((c & 7) ^ (t & 7)) << 4);
+  }
+};
+
+// Per-warp flash state for 16 rows: thread holds rows lane/4 and lane/4+8.
+// C gives the shared-memory layout of a K or V chunk.
+template <int HD, class C = ChunkLayout<HD>>
 struct Flash {
   float o[HD / 8][4];
   float m[2], l[2];
@@ -114,7 +129,6 @@ struct Flash {
   __device__ __forceinline__ void step(const uint32_t (*qa)[4], uint32_t sk, uint32_t sv,
                                        int chunk, int ctx, const int* limit, float scale_log2,
                                        int lane) {
-    using C = ChunkLayout<HD>;
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
@@ -213,12 +227,68 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, int q0, int G, int kvh
   }
 }
 
+// Merge the per-warp flash states of nw warps (smem: O[nw][16][HD] fp32,
+// m[nw][16], l[nw][16]) and write the normalised rows: straight to `out`
+// when the sequence has one split, else (O/l, max + log2 l) to the split
+// workspace.  Called by every thread of the CTA after the key loop.
+template <int HD, class F>
+__device__ __forceinline__ void merge_warps(const AttnArgs& a, F& f, uint8_t* smem, int nw,
+                                            int warp, int lane, int seq, int kvh, int split,
+                                            int n_splits, int q0, int G, int nrows,
+                                            bool participates) {
+  constexpr int LD = HD + 4;  // padded rows: no bank conflicts on the fragment stores
+  float* so = reinterpret_cast<float*>(smem);
+  float* sm = so + nw * 16 * LD;
+  float* sl = sm + nw * 16;
+  if (participates) {
+    const int g4 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = g4 + (e >> 1) * 8, c = nt * 8 + 2 * t4 + (e & 1);
+        so[(warp * 16 + r) * LD + c] = f.o[nt][e];
+      }
+    if (t4 == 0) {
+      sm[warp * 16 + g4] = f.m[0];
+      sm[warp * 16 + g4 + 8] = f.m[1];
+      sl[warp * 16 + g4] = f.l[0];
+      sl[warp * 16 + g4 + 8] = f.l[1];
+    }
+  }
+  __syncthreads();
+  const bool direct = n_splits == 1;
+  for (int i = threadIdx.x; i < nrows * HD; i += blockDim.x) {
+    const int r = i / HD, c = i % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < nw; ++w) M = fmaxf(M, sm[w * 16 + r]);
+    const float mu = M == -INFINITY ? 0.f : M;
+    float L = 0.f, acc = 0.f;
+    for (int w = 0; w < nw; ++w) {
+      const float sc = exp2f(sm[w * 16 + r] - mu);
+      L += sl[w * 16 + r] * sc;
+      acc += so[(w * 16 + r) * LD + c] * sc;
+    }
+    const float val = L > 0.f ? acc / L : 0.f;
+    if (direct) {
+      a.out[(size_t)(q0 + r / G) * a.ld_out + (size_t)(kvh * G + r % G) * HD + c] =
+          __float2bfloat16_rn(val);
+    } else {
+      const size_t base = (((size_t)seq * a.n_kv_heads + kvh) * a.max_splits + split) * 16 + r;
+      a.ws_o[base * HD + c] = val;
+      if (c == 0) a.ws_lse[base] = L > 0.f ? mu + log2f(L) : -INFINITY;
+    }
+  }
+}
+
 constexpr int DEC_STAGES = 3;
 
 template <int HD>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   using C = ChunkLayout<HD>;
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
@@ -276,58 +346,133 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   cp_wait<0>();
   f.finish_sum();
   __syncthreads();
+  merge_warps<HD>(a, f, smem, 4, warp, lane, seq, kvh, split, n_splits, q0, G, nrows, true);
+}
 
-  // merge the 4 warps: smem reused as O[4][16][HD], m[4][16], l[4][16]
-  float* so = reinterpret_cast<float*>(smem);
-  float* sm = so + 4 * 16 * HD;
-  float* sl = sm + 4 * 16;
-  {
-    const int g4 = lane >> 2, t4 = lane & 3;
-#pragma unroll
-    for (int nt = 0; nt < HD / 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = g4 + (e >> 1) * 8, c = nt * 8 + 2 * t4 + (e & 1);
-        so[(warp * 16 + r) * HD + c] = f.o[nt][e];
-      }
-    if (t4 == 0) {
-      sm[warp * 16 + g4] = f.m[0];
-      sm[warp * 16 + g4 + 8] = f.m[1];
-      sl[warp * 16 + g4] = f.l[0];
-      sl[warp * 16 + g4 + 8] = f.l[1];
+// Decode attention with TMA key/value loads (head_dim 64 or 128, block size a
+// multiple of 16).  Warp 4 issues, for every 16-token chunk of the split, one
+// 2-D TMA box per 64-column half of K and of V straight from the pool (the
+// pool viewed as [num_blocks*2*n_kv*bs rows, hd]), into an 8-slot ring guarded
+// by mbarriers; warps 0-3 consume chunks round-robin and merge at the end.
+constexpr int TMA_STAGES = 8;
+constexpr int TMA_THREADS = 160;
+constexpr int TMA_MAX_SPLIT_CHUNKS = 128;   // split_tokens <= 2048
+// Chunk i goes to slot i % TMA_STAGES and to consumer warp i % 4.  With the
+// stage count a multiple of 4 every slot has a single consumer warp, which
+// waits on its slot's phases strictly in order; otherwise a warp could wait
+// for a phase two ahead of the slot's current one, and mbarrier parity waits
+// cannot tell those apart.
+static_assert(TMA_STAGES % 4 == 0, "each ring slot must belong to one consumer warp");
+
+template <int HD>
+__global__ void __launch_bounds__(TMA_THREADS, 3)
+    attn_decode_tma_kernel(const __grid_constant__ CUtensorMap pool_map, const AttnArgs a) {
+  using C = TmaChunkLayout<HD>;
+  constexpr int SLOT = 2 * C::BYTES;  // K then V
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TMA_STAGES * SLOT);
+  uint64_t* empty = full + TMA_STAGES;
+  int* chunk_row = reinterpret_cast<int*>(empty + TMA_STAGES);  // [split_chunks] pool row of K
+
+  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // step metadata and block tables come from host copies, not from the
+  // previous kernel: read them before waiting
+  const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
+  const int G = a.n_q_heads / a.n_kv_heads;
+  const int nrows = qlen * G;
+  const int n_chunks = (ctx + 15) / 16;
+  const int n_splits = (n_chunks + a.split_chunks - 1) / a.split_chunks;
+  if (threadIdx.x == 0) pdl_trigger();
+  if (split >= n_splits || nrows <= 0) {
+    pdl_wait();
+    return;
+  }
+  if (nrows > 16) {
+    pdl_wait();
+    if (threadIdx.x == 0) set_status(ERR_BAD_INDEX);
+    return;
+  }
+  const int c_begin = split * a.split_chunks;
+  const int n_mine = min(c_begin + a.split_chunks, n_chunks) - c_begin;
+  const int* table = a.block_tables + (size_t)seq * a.bt_ld;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TMA_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
+    fence_mbar_init();
   }
   __syncthreads();
-  const bool direct = n_splits == 1;
-  for (int i = threadIdx.x; i < nrows * HD; i += blockDim.x) {
-    const int r = i / HD, c = i % HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
-    const float mu = M == -INFINITY ? 0.f : M;
-    float L = 0.f, acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float sc = exp2f(sm[w * 16 + r] - mu);
-      L += sl[w * 16 + r] * sc;
-      acc += so[(w * 16 + r) * HD + c] * sc;
+
+  Flash<HD, C> f;
+  f.init();
+  if (warp == 4) {
+    // ---- producer: the split's pool rows first (one coalesced pass over the
+    // block table), then one TMA box per K/V half per chunk
+    for (int i = lane; i < n_mine; i += 32) {
+      const int p0 = (c_begin + i) * 16;
+      int blk = table[p0 / a.block_size];
+      if (blk < 0 || blk >= a.num_blocks) {
+        set_status(ERR_BAD_INDEX);
+        blk = 0;  // load something valid; the result is flagged
+      }
+      chunk_row[i] = ((blk * 2) * a.n_kv_heads + kvh) * a.block_size + p0 % a.block_size;
     }
-    const float val = L > 0.f ? acc / L : 0.f;
-    if (direct) {
-      a.out[(size_t)(q0 + r / G) * a.ld_out + (size_t)(kvh * G + r % G) * HD + c] =
-          __float2bfloat16_rn(val);
-    } else {
-      const size_t base = (((size_t)seq * a.n_kv_heads + kvh) * a.max_splits + split) * 16 + r;
-      a.ws_o[base * HD + c] = val;
-      if (c == 0) a.ws_lse[base] = L > 0.f ? mu + log2f(L) : -INFINITY;
+    __syncwarp();
+    pdl_wait();   // K/V of this step are written by the preceding QKV kernel
+    if (lane == 0) {
+      prefetch_tmap(&pool_map);
+      const int rows_per_kv = a.n_kv_heads * a.block_size;
+      for (int i = 0; i < n_mine; ++i) {
+        const int s = i % TMA_STAGES;
+        if (i >= TMA_STAGES && !mbar_wait(&empty[s], ((i / TMA_STAGES) - 1) & 1)) break;
+        const int row_k = chunk_row[i];
+        uint8_t* dst = smem + s * SLOT;
+        mbar_arrive_expect_tx(&full[s], SLOT);
+#pragma unroll
+        for (int hf = 0; hf < HD / 64; ++hf) {
+          tma_load_2d(dst + hf * 2048, &pool_map, &full[s], hf * 64, row_k);
+          tma_load_2d(dst + C::BYTES + hf * 2048, &pool_map, &full[s], hf * 64, row_k + rows_per_kv);
+        }
+      }
     }
+  } else {
+    // ---- consumers: warp w takes chunks w, w+4, ...
+    pdl_wait();
+    uint32_t qa[HD / 16][4];
+    load_q<HD>(a, q0, G, kvh, 0, nrows, lane, qa);
+    int limit[2];
+    const int first = ctx - qlen;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = min((lane >> 2) + 8 * h, nrows - 1);
+      limit[h] = first + r / G;
+    }
+    const uint32_t base = smem_u32(smem);
+    for (int i = warp; i < n_mine; i += 4) {
+      const int s = i % TMA_STAGES;
+      if (!mbar_wait(&full[s], (i / TMA_STAGES) & 1)) break;
+      const uint32_t sk = base + s * SLOT;
+      f.step(qa, sk, sk + C::BYTES, c_begin + i, ctx, limit, a.scale_log2, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    f.finish_sum();
   }
+  __syncthreads();   // ring drained: every issued load was consumed
+  merge_warps<HD>(a, f, smem, 4, warp, lane, seq, kvh, split, n_splits, q0, G, nrows, warp < 4);
 }
 
 // Merge decode splits: one CTA per (kv head, seq); skips sequences that fit
 // one split (their output was written directly).
 template <int HD>
 __global__ void attn_combine_kernel(const AttnArgs a) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const int kvh = blockIdx.x, seq = blockIdx.y;
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
@@ -358,6 +503,8 @@ template <int HD>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
   using C = ChunkLayout<HD>;
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const int seq = a.work[2 * blockIdx.x], rt = a.work[2 * blockIdx.x + 1];
   const int kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -422,9 +569,38 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
 // ------------------------------------------------------------------ host side
 
 template <int HD>
+static int decode_tma_launch(const AttnArgs& a, cudaStream_t st) {
+  constexpr int SLOT = 2 * TmaChunkLayout<HD>::BYTES;
+  const int merge = (4 * 16 * (HD + 4) + 2 * 4 * 16) * 4;
+  const int ring = TMA_STAGES * SLOT + 2 * TMA_STAGES * 8 + TMA_MAX_SPLIT_CHUNKS * 4;
+  const int smem = (ring > merge ? ring : merge) + 1024;
+  if (a.split_chunks > TMA_MAX_SPLIT_CHUNKS) return arg_err("split_tokens above 2048");
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_tma_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_decode_tma_kernel<HD>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return host_err(e, "attention smem attribute");
+    attr = true;
+  }
+  CUtensorMap map;
+  const uint64_t rows = (uint64_t)a.num_blocks * 2 * a.n_kv_heads * a.block_size;
+  int rc = make_tmap_2d(&map, a.pool, HD, rows, (uint64_t)HD * 2, 64, 16);
+  if (rc) return rc;
+  rc = launch_pdl(attn_decode_tma_kernel<HD>, dim3(a.max_splits, a.n_kv_heads, a.n_seqs),
+                  dim3(TMA_THREADS), smem, st, 1, "attention decode launch", map, a);
+  if (rc || a.max_splits <= 1) return rc;
+  return launch_pdl(attn_combine_kernel<HD>, dim3(a.n_kv_heads, a.n_seqs), dim3(128), 0, st, 1,
+                    "attention combine launch", a);
+}
+
+template <int HD>
 static int decode_launch(const AttnArgs& a, cudaStream_t st) {
   const int smem_ring = 4 * DEC_STAGES * 2 * ChunkLayout<HD>::BYTES;
-  const int smem_merge = (4 * 16 * HD + 2 * 4 * 16) * 4;
+  const int smem_merge = (4 * 16 * (HD + 4) + 2 * 4 * 16) * 4;
   const int smem = smem_ring > smem_merge ? smem_ring : smem_merge;
   static bool attr = false;
   if (!attr) {
@@ -433,19 +609,18 @@ static int decode_launch(const AttnArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return host_err(e, "attention smem attribute");
     attr = true;
   }
-  dim3 grid(a.max_splits, a.n_kv_heads, a.n_seqs);
-  attn_decode_kernel<HD><<<grid, 128, smem, st>>>(a);
-  int rc = host_err(cudaGetLastError(), "attention decode launch");
+  int rc = launch_pdl(attn_decode_kernel<HD>, dim3(a.max_splits, a.n_kv_heads, a.n_seqs),
+                      dim3(128), smem, st, 1, "attention decode launch", a);
   if (rc || a.max_splits <= 1) return rc;
-  attn_combine_kernel<HD><<<dim3(a.n_kv_heads, a.n_seqs), 128, 0, st>>>(a);
-  return host_err(cudaGetLastError(), "attention combine launch");
+  return launch_pdl(attn_combine_kernel<HD>, dim3(a.n_kv_heads, a.n_seqs), dim3(128), 0, st, 1,
+                    "attention combine launch", a);
 }
 
 template <int HD>
 static int prefill_launch(const AttnArgs& a, int n_work, cudaStream_t st) {
   const int smem = PF_STAGES * 2 * ChunkLayout<HD>::BYTES;
-  attn_prefill_kernel<HD><<<dim3(n_work, a.n_kv_heads), 128, smem, st>>>(a);
-  return host_err(cudaGetLastError(), "attention prefill launch");
+  return launch_pdl(attn_prefill_kernel<HD>, dim3(n_work, a.n_kv_heads), dim3(128), smem, st, 1,
+                    "attention prefill launch", a);
 }
 
 static int check_common(const AttnArgs& a, int head_dim) {
@@ -464,10 +639,12 @@ int attn_decode(AttnArgs a, int head_dim, cudaStream_t st) {
   if (a.max_splits > 1 && (a.ws_o == nullptr || a.ws_lse == nullptr)) return arg_err("split workspace");
   if (a.n_seqs == 0) return TB_OK;
   a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  // TMA boxes need 16-token chunks inside one block and a 16-byte aligned pool
+  const bool tma = a.block_size % 16 == 0 && reinterpret_cast<uintptr_t>(a.pool) % 16 == 0;
   switch (head_dim) {
     case 16: return decode_launch<16>(a, st);
-    case 64: return decode_launch<64>(a, st);
-    default: return decode_launch<128>(a, st);
+    case 64: return tma ? decode_tma_launch<64>(a, st) : decode_launch<64>(a, st);
+    default: return tma ? decode_tma_launch<128>(a, st) : decode_launch<128>(a, st);
   }
 }
 

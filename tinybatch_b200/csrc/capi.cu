@@ -34,7 +34,7 @@ size_t tiles_of(int M, int N, int bn) {
 int gemm_scratch(GemmArgs& g, int bn, void* ws, size_t ws_bytes) {
   g.ws = nullptr;
   g.counters = nullptr;
-  if (g.splits <= 1) return TB_OK;
+  if (g.splits <= 1 || ws == nullptr) return TB_OK;  // no scratch: cluster split-K
   const size_t tiles = tiles_of(g.M, g.N, bn);
   if (tiles > COUNTER_TILES) return arg_err("split-K over more than 16384 tiles");
   const size_t need = COUNTER_BYTES + tiles * g.splits * bn * 128 * sizeof(float);
@@ -61,7 +61,7 @@ GemmArgs base_args(int M, int N, int K, int splits, const float* sq, int sq_part
   return g;
 }
 
-bool valid_bn(int bn) { return bn == 64 || bn == 128 || bn == 256; }
+bool valid_bn(int bn) { return bn == 64 || bn == 128 || bn == 192 || bn == 256; }
 
 }  // namespace
 
@@ -81,6 +81,11 @@ int tb_status(unsigned int* code_h, int clear) {
   return host_err(cudaMemcpyToSymbol(g_status, &zero, sizeof(unsigned int)), "status clear");
 }
 
+int tb_gemm_max_active_clusters(int bn, int cluster, int* out_h) {
+  if (out_h == nullptr || cluster < 1 || cluster > 8) return arg_err("cluster must be 1..8");
+  return gemm_max_active_clusters(bn, cluster, out_h);
+}
+
 size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits) {
   if (splits <= 1) return 0;
   const size_t tiles = tiles_of(M, N, bn);
@@ -91,7 +96,7 @@ int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int 
               const float* sq, int sq_parts, int sq_ld, float inv_d, float eps, void* out,
               int ld_out, int out_f32, int bn, int splits, void* ws, size_t ws_bytes,
               void* stream) {
-  if (!valid_bn(bn)) return arg_err("bn must be 64, 128 or 256");
+  if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (out == nullptr || ld_out < N || (out_f32 ? ld_out % 4 : ld_out % 8))
     return arg_err("out / ld_out");
   GemmArgs g = base_args(M, N, K, splits, sq, sq_parts, sq_ld, inv_d, eps);
@@ -110,7 +115,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
                    void* q_out, int ld_q, void* kv_pool, int block_size, int bn, int splits,
                    void* ws, size_t ws_bytes, void* stream) {
   if (!valid_bn(bn) || head_dim <= 0 || head_dim % 16 || bn % head_dim)
-    return arg_err("bn must be 64/128/256 and a multiple of head_dim (multiple of 16)");
+    return arg_err("bn must be 64/128/192/256 and a multiple of head_dim (multiple of 16)");
   if (bias == nullptr || rope_cos == nullptr || rope_sin == nullptr || positions == nullptr ||
       slots == nullptr || q_out == nullptr || kv_pool == nullptr)
     return arg_err("null pointer");
@@ -140,7 +145,7 @@ int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, 
                       int n_feat, const float* sq, int sq_parts, int sq_ld, float inv_d,
                       float eps, void* act, int ld_act, int bn, int splits, void* ws,
                       size_t ws_bytes, void* stream) {
-  if (!valid_bn(bn)) return arg_err("bn must be 64, 128 or 256");
+  if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (n_feat <= 0 || n_feat % 16 || ld_act < n_feat || ld_act % 8 || act == nullptr)
     return arg_err("n_feat must be a multiple of 16; act / ld_act");
   const int half = bn / 2;
@@ -159,7 +164,7 @@ int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M
                            float* sq_out, int sq_out_ld, const int* row_dst, void* hg2,
                            float* sq2, int sq2_ld, int bn, int splits, void* ws,
                            size_t ws_bytes, void* stream) {
-  if (!valid_bn(bn)) return arg_err("bn must be 64, 128 or 256");
+  if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (N % 16 || h == nullptr || g_next == nullptr || hg == nullptr || sq_out == nullptr)
     return arg_err("N must be a multiple of 16; h / g_next / hg / sq_out");
   if (ld_h < N || ld_h % 4 || ld_hg < N || ld_hg % 8 || sq_out_ld < M)

@@ -38,6 +38,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Wait budget: 2 s of wall time, checked every 4096 polls.
 constexpr uint64_t WAIT_BUDGET_NS = 2000000000ull;
 
+// ------------------------------------------------- programmatic dependent launch
+//
+// Every kernel of the library is launched with programmatic stream
+// serialisation, so it may start while the previous kernel in the stream is
+// still finishing.  Rules each kernel follows:
+//   pdl_trigger()  once per CTA after setup: lets the next kernel launch as
+//                  soon as every CTA of this grid is running;
+//   pdl_wait()     before the first access (read or write) to memory an
+//                  earlier kernel uses, and on every path of every CTA
+//                  before it exits, so that this grid completing still
+//                  implies its predecessors completed.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ mbarrier
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

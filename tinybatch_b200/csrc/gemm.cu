@@ -11,14 +11,27 @@ constexpr int BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int GEMM_THREADS = 192;
 
+// How a split-K launch combines its partial accumulators.
+enum SplitMode : int {
+  SPLIT_NONE = 0,     // one CTA per tile
+  SPLIT_GLOBAL = 1,   // partials in caller scratch; last CTA to arrive reduces
+  SPLIT_CLUSTER = 2,  // the splits of a tile form a thread-block cluster; each
+                      // CTA parks its partial in its own shared memory and
+                      // reduces a slice of columns over DSMEM
+};
+
+constexpr int tmem_cols(int bn) { return bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256; }
+
 template <int BN, int STAGES>
 struct GemmLayout {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = STAGES * A_BYTES;
   static constexpr int OFF_BAR = OFF_B + STAGES * B_BYTES;
-  static constexpr int BAR_BYTES = (2 * STAGES + 1) * 8 + 16;
-  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int BAR_BYTES = (2 * STAGES + 1) * 8 + 16 + BM * 4;  // + per-row sums
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;                // + alignment slack
+  // cluster mode parks the fp32 tile [BN/4][BM] float4 over the stage ring
+  static_assert(BN * BM * 4 <= OFF_BAR, "stage ring too small for the partial tile");
 };
 
 __device__ __forceinline__ float row_scale(const GemmArgs& g, int m) {
@@ -28,19 +41,65 @@ __device__ __forceinline__ float row_scale(const GemmArgs& g, int m) {
   return rsqrtf(s * g.inv_d + g.eps);
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // Accumulator access for the epilogue: columns [c, c+W) of this thread's row.
-// Collective over the warp (tcgen05.ld is .sync.aligned): every lane calls it.
+// In SPLIT_NONE / SPLIT_GLOBAL mode it reads TMEM (collective over the warp:
+// every lane calls it); in SPLIT_CLUSTER mode it sums the cluster's parked
+// partial tiles in rank order.
 template <int BN>
 struct AccReader {
   uint32_t taddr;   // TMEM address of this warp's lane quarter, column 0
-  int splits, z, row;
-  const float* ws;  // this tile's workspace, [splits][BN][128]
+  int mode, splits, z, row;
+  const float* ws;  // SPLIT_GLOBAL: this tile's workspace, [splits][BN][128]
+  uint32_t red;     // SPLIT_CLUSTER: shared address of the parked tile
   template <int W>
   __device__ __forceinline__ void load(int c, float* v) const {
+    if (mode == SPLIT_CLUSTER) {
+#pragma unroll
+      for (int j = 0; j < W; ++j) v[j] = 0.f;
+      for (int s = 0; s < splits; ++s) {
+        const uint32_t base = cluster_map(red, s);
+#pragma unroll
+        for (int i = 0; i < W / 4; ++i) {
+          const float4 x = ld_cluster_v4(base + (uint32_t)(((c / 4 + i) * BM + row) * 16));
+          v[4 * i] += x.x;
+          v[4 * i + 1] += x.y;
+          v[4 * i + 2] += x.z;
+          v[4 * i + 3] += x.w;
+        }
+      }
+      return;
+    }
     float own[W];
     if constexpr (W == 16) tmem_ld16(taddr + c, own);
     else tmem_ld8(taddr + c, own);
-    if (splits == 1) {
+    if (mode == SPLIT_NONE) {
 #pragma unroll
       for (int j = 0; j < W; ++j) v[j] = own[j];
       return;
@@ -62,15 +121,21 @@ struct AccReader {
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// The fused epilogue for this thread's row.  Work is divided in units (a
+// 16-column chunk; a head for EPI_QKV); this CTA handles the units u with
+// u % n_own == own (all units unless the tile is split over a cluster).
+// EPI_RESID returns the row's sum of h^2 over the handled columns.
 template <int BN, int EPI>
-__device__ __forceinline__ void run_epilogue(const GemmArgs& g, const AccReader<BN>& acc,
-                                             int tm, int tn, int row) {
+__device__ __forceinline__ float run_epilogue(const GemmArgs& g, const AccReader<BN>& acc, int tm,
+                                              int tn, int row, int own, int n_own) {
   const int m = tm * BM + row;
   const bool valid = m < g.M;
   const float rs = row_scale(g, m);
+  float ss = 0.f;
 
   if constexpr (EPI == EPI_F32 || EPI == EPI_BF16) {
-    for (int c = 0; c < BN; c += 16) {
+    for (int u = own; u < BN / 16; u += n_own) {
+      const int c = u * 16;
       const int n = tn * BN + c;
       if (n >= g.N) break;
       float v[16];
@@ -101,7 +166,8 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& g, const AccReader<
   } else if constexpr (EPI == EPI_SWIGLU) {
     // Tile tn holds features [tn*BN/2, (tn+1)*BN/2): gate rows first, up rows second.
     constexpr int HALF = BN / 2;
-    for (int c = 0; c < HALF; c += 16) {
+    for (int u = own; u < HALF / 16; u += n_own) {
+      const int c = u * 16;
       const int f = tn * HALF + c;
       if (f >= g.n_feat) break;
       float gv[16], uv[16];
@@ -119,9 +185,9 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& g, const AccReader<
       store_bf16x8(o + 8, y + 8);
     }
   } else if constexpr (EPI == EPI_RESID) {
-    float ss = 0.f;
     const int dst = (valid && g.row_dst != nullptr) ? g.row_dst[m] : -1;
-    for (int c = 0; c < BN; c += 16) {
+    for (int u = own; u < BN / 16; u += n_own) {
+      const int c = u * 16;
       const int n = tn * BN + c;
       if (n >= g.N) break;
       float v[16];
@@ -159,10 +225,6 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& g, const AccReader<
         store_bf16x8(p2 + 8, o + 8);
       }
     }
-    if (valid) {
-      g.sq_out[(size_t)tn * g.sq_out_ld + m] = ss;
-      if (dst >= 0) g.sq2[(size_t)tn * g.sq2_ld + dst] = ss;
-    }
   } else if constexpr (EPI == EPI_QKV) {
     const int hd = g.head_dim, half = hd >> 1;
     const int heads_in_tile = BN / hd;
@@ -179,7 +241,7 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& g, const AccReader<
     }
     const int blk = slot >= 0 ? slot / g.block_size : 0;
     const int off = slot >= 0 ? slot % g.block_size : 0;
-    for (int hh = 0; hh < heads_in_tile; ++hh) {
+    for (int hh = own; hh < heads_in_tile; hh += n_own) {
       const int head = tn * heads_in_tile + hh;
       if (head >= total_heads) break;
       const int c0 = hh * hd;
@@ -230,6 +292,19 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& g, const AccReader<
       }
     }
   }
+  return ss;
+}
+
+// Row sum of h^2 for the whole tile -> sq_out (and sq2 for gathered rows).
+__device__ __forceinline__ void store_row_sumsq(const GemmArgs& g, int tm, int tn, int row,
+                                                float ss) {
+  const int m = tm * BM + row;
+  if (m >= g.M) return;
+  g.sq_out[(size_t)tn * g.sq_out_ld + m] = ss;
+  if (g.row_dst != nullptr) {
+    const int dst = g.row_dst[m];
+    if (dst >= 0) g.sq2[(size_t)tn * g.sq2_ld + dst] = ss;
+  }
 }
 
 template <int BN, int STAGES, int EPI>
@@ -237,6 +312,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
                    const __grid_constant__ CUtensorMap tma_b, const GemmArgs g) {
   using L = GemmLayout<BN, STAGES>;
+  constexpr uint32_t TCOLS = tmem_cols(BN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -247,17 +323,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* done = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* row_ss = reinterpret_cast<float*>(tmem_slot + 4);  // [BM] per-row partial sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mode = g.splits == 1 ? SPLIT_NONE : (g.ws != nullptr ? SPLIT_GLOBAL : SPLIT_CLUSTER);
 
   // grouped raster: m fastest inside a group of group_m row tiles
-  const int tile = blockIdx.x;
+  const int tile = mode == SPLIT_CLUSTER ? (int)blockIdx.x / g.splits : (int)blockIdx.x;
+  const int z = mode == SPLIT_CLUSTER ? (int)blockIdx.x % g.splits : (int)blockIdx.y;
   const int per_group = g.group_m * g.tiles_n;
   const int first_m = (tile / per_group) * g.group_m;
   const int gsize = min(g.tiles_m - first_m, g.group_m);
   const int tm = first_m + (tile % per_group) % gsize;
   const int tn = (tile % per_group) / gsize;
-  const int z = blockIdx.y;
   const int num_k = (g.K + BK - 1) / BK;
   const int kb = (int)((long long)z * num_k / g.splits);
   const int ke = (int)((long long)(z + 1) * num_k / g.splits);
@@ -273,19 +351,30 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     prefetch_tmap(&tma_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, TCOLS);
     tmem_relinquish();
     tc_fence_before();
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer
-    for (int it = kb; it < ke; ++it) {
+    // The weight tiles of the first stages do not depend on earlier kernels:
+    // fetch them before waiting for the previous kernel, then the activations.
+    const int pre = min(STAGES, ke - kb);
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], A_BYTES + L::B_BYTES);
+      tma_load_2d(sB + i * L::B_BYTES, &tma_b, &full[i], (kb + i) * BK, tn * BN);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(sA + i * A_BYTES, &tma_a, &full[i], (kb + i) * BK, tm * BM);
+    for (int it = kb + pre; it < ke; ++it) {
       const int i = it - kb, s = i % STAGES;
-      if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) break;
+      if (!mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) break;
       mbar_arrive_expect_tx(&full[s], A_BYTES + L::B_BYTES);
       tma_load_2d(sA + s * A_BYTES, &tma_a, &full[s], it * BK, tm * BM);
       tma_load_2d(sB + s * L::B_BYTES, &tma_b, &full[s], it * BK, tn * BN);
@@ -310,20 +399,61 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     if (ok) tc_commit(done);
     else mbar_arrive(done);
+  }
+  __syncwarp();
+
+  const int q = warp & 3;
+  const int row = q * 32 + lane;
+  AccReader<BN> acc;
+  acc.taddr = tmem_base + ((uint32_t)(q * 32) << 16);
+  acc.mode = mode;
+  acc.splits = g.splits;
+  acc.z = z;
+  acc.row = row;
+  acc.ws = nullptr;
+  acc.red = smem_u32(smem);
+
+  if (warp >= 2) pdl_wait();   // the epilogue reads and writes buffers earlier kernels use
+  if (mode == SPLIT_CLUSTER) {
+    // 1. park this CTA's fp32 partial over its (idle) stage ring as
+    //    float4 [BN/4][BM]; every MMA and TMA write has completed once
+    //    `done` fires, so the ring is free
+    if (warp >= 2) {
+      mbar_wait(done, 0);
+      tc_fence_after();
+      float4* red = reinterpret_cast<float4*>(smem);
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(acc.taddr + c, v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          red[(c / 4 + i) * BM + row] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    cluster_sync_all();
+    // 2. reduce this CTA's share of the columns across the cluster and run
+    //    the epilogue on it
+    float ss = 0.f;
+    if (warp >= 2) ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, z, g.splits);
+    if constexpr (EPI == EPI_RESID) {
+      if (warp >= 2) row_ss[row] = ss;
+    }
+    cluster_sync_all();
+    // 3. rank 0 of the cluster combines the per-row sums of h^2
+    if constexpr (EPI == EPI_RESID) {
+      if (warp >= 2 && z == 0) {
+        float tot = 0.f;
+        const uint32_t a = smem_u32(row_ss + row);
+        for (int s = 0; s < g.splits; ++s) tot += ld_cluster_f32(cluster_map(a, s));
+        store_row_sumsq(g, tm, tn, row, tot);
+      }
+    }
+    cluster_sync_all();
   } else if (warp >= 2) {
-    // ---------------- epilogue
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
     mbar_wait(done, 0);
     tc_fence_after();
-    AccReader<BN> acc;
-    acc.taddr = tmem_base + ((uint32_t)(q * 32) << 16);
-    acc.splits = g.splits;
-    acc.z = z;
-    acc.row = row;
-    acc.ws = nullptr;
     bool run = true;
-    if (g.splits > 1) {
+    if (mode == SPLIT_GLOBAL) {
       const size_t tile_lin = (size_t)tm * g.tiles_n + tn;
       float* ws_tile = g.ws + tile_lin * g.splits * BN * BM;
       float* mine = ws_tile + (size_t)z * BN * BM + row;
@@ -346,14 +476,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __threadfence();
       acc.ws = ws_tile;
     }
-    if (run) run_epilogue<BN, EPI>(g, acc, tm, tn, row);
+    if (run) {
+      const float ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, 0, 1);
+      if constexpr (EPI == EPI_RESID) store_row_sumsq(g, tm, tn, row, ss);
+    }
   }
 
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, BN);
+    tmem_dealloc(tmem_base, TCOLS);
   }
 }
 
@@ -370,9 +503,12 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const GemmAr
     if (e != cudaSuccess) return host_err(e, "gemm smem attribute");
     attr_set = true;
   }
-  dim3 grid(g.tiles_m * g.tiles_n, g.splits);
-  kern<<<grid, GEMM_THREADS, L::SMEM, stream>>>(ta, tb_, g);
-  return host_err(cudaGetLastError(), "gemm launch");
+  const int tiles = g.tiles_m * g.tiles_n;
+  if (g.splits > 1 && g.ws == nullptr)  // cluster split-K: a tile's splits are one cluster along x
+    return launch_pdl(kern, dim3(tiles * g.splits), dim3(GEMM_THREADS), L::SMEM, stream,
+                      g.splits, "gemm cluster launch", ta, tb_, g);
+  return launch_pdl(kern, dim3(tiles, g.splits), dim3(GEMM_THREADS), L::SMEM, stream, 1,
+                    "gemm launch", ta, tb_, g);
 }
 
 template <int EPI>
@@ -381,19 +517,55 @@ static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_, con
   switch (bn) {
     case 64: return launch_bn<64, 8, EPI>(ta, tb_, g, stream);
     case 128: return launch_bn<128, 6, EPI>(ta, tb_, g, stream);
+    case 192: return launch_bn<192, 5, EPI>(ta, tb_, g, stream);
     case 256: return launch_bn<256, 4, EPI>(ta, tb_, g, stream);
-    default: return TB_ERR_ARG;
+    default: return arg_err("bn must be 64, 128, 192 or 256");
+  }
+}
+
+template <int BN, int STAGES>
+static int max_clusters_bn(int cluster, int* out) {
+  using L = GemmLayout<BN, STAGES>;
+  auto kern = gemm_tc_kernel<BN, STAGES, EPI_F32>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+  if (e != cudaSuccess) return host_err(e, "gemm smem attribute");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster * 64, 1, 1);
+  cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = L::SMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return host_err(cudaOccupancyMaxActiveClusters(out, kern, &cfg), "max active clusters");
+}
+
+int gemm_max_active_clusters(int bn, int cluster, int* out) {
+  switch (bn) {
+    case 64: return max_clusters_bn<64, 8>(cluster, out);
+    case 128: return max_clusters_bn<128, 6>(cluster, out);
+    case 192: return max_clusters_bn<192, 5>(cluster, out);
+    case 256: return max_clusters_bn<256, 4>(cluster, out);
+    default: return arg_err("bn must be 64, 128, 192 or 256");
   }
 }
 
 int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb, GemmArgs g,
                 cudaStream_t stream) {
-  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return TB_ERR_ARG;
-  if ((lda * 2) % 16 || (ldb * 2) % 16 || lda < g.K || ldb < g.K) return TB_ERR_ARG;
-  if (reinterpret_cast<uintptr_t>(A) % 16 || reinterpret_cast<uintptr_t>(B) % 16) return TB_ERR_ARG;
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return arg_err("M, N, K must be positive");
+  if ((lda * 2) % 16 || (ldb * 2) % 16 || lda < g.K || ldb < g.K)
+    return arg_err("lda/ldb: rows must be 16-byte multiples and >= K");
+  if (reinterpret_cast<uintptr_t>(A) % 16 || reinterpret_cast<uintptr_t>(B) % 16)
+    return arg_err("A and B must be 16-byte aligned");
   const int num_k = (g.K + BK - 1) / BK;
-  if (g.splits < 1 || g.splits > num_k) return TB_ERR_ARG;
-  if (g.splits > 1 && (g.ws == nullptr || g.counters == nullptr)) return TB_ERR_ARG;
+  if (g.splits < 1 || g.splits > num_k) return arg_err("splits must be in [1, ceil(K/64)]");
+  if (g.splits > 1 && g.ws == nullptr && g.splits > 8)
+    return arg_err("cluster split-K supports at most 8 splits");
+  if (g.splits > 1 && (g.ws == nullptr) != (g.counters == nullptr))
+    return arg_err("split-K scratch pointers");
   g.tiles_m = (g.M + BM - 1) / BM;
   g.tiles_n = (g.N + bn - 1) / bn;
   if (g.group_m <= 0) g.group_m = 16;
@@ -408,14 +580,8 @@ int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb,
     case EPI_QKV: return launch_epi<EPI_QKV>(bn, ta, tbm, g, stream);
     case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(bn, ta, tbm, g, stream);
     case EPI_RESID: return launch_epi<EPI_RESID>(bn, ta, tbm, g, stream);
-    default: return TB_ERR_ARG;
+    default: return arg_err("unknown epilogue");
   }
-}
-
-size_t gemm_workspace_bytes(int M, int N, int bn, int splits) {
-  if (splits <= 1) return 0;
-  const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-  return tiles * splits * bn * BM * sizeof(float);
 }
 
 }  // namespace tb

@@ -8,6 +8,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/tinybatch_b200.h"
 
 namespace tb {
@@ -23,9 +25,36 @@ void set_last_error(const char* fmt, ...);
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                  uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_rows);
 
+// Launch `kern` on `stream` with programmatic stream serialisation (PDL) and,
+// when cluster_x > 1, a (cluster_x, 1, 1) thread-block cluster.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               int cluster_x, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return host_err(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
+}
+
 struct GemmArgs;
 int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb, GemmArgs g,
                 cudaStream_t stream);
-size_t gemm_workspace_bytes(int M, int N, int bn, int splits);
+int gemm_max_active_clusters(int bn, int cluster, int* out);
 
 }  // namespace tb

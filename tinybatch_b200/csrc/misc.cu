@@ -10,6 +10,8 @@ __global__ void __launch_bounds__(128) embed_kernel(const int* ids, const __nv_b
                                                     const __nv_bfloat16* g, float* h, int ld_h,
                                                     __nv_bfloat16* hg, int ld_hg, float* sq) {
   __shared__ float red[4];
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const int m = blockIdx.x;
   int id = ids[m];
   if (id < 0 || id >= vocab) {
@@ -50,6 +52,8 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
 __global__ void __launch_bounds__(512) argmax_kernel(const float* logits, int ld, int N, int* out) {
   __shared__ float sv[16];
   __shared__ int si[16];
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
   const float* row = logits + (size_t)blockIdx.x * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
@@ -91,16 +95,16 @@ int embed_launch(const int* ids, int M, const void* emb, int ld_emb, int d, int 
                  cudaStream_t st) {
   if (M < 0 || d <= 0 || d % 8 || ld_emb % 8 || ld_h % 4 || ld_hg % 8) return arg_err("embed shapes");
   if (M == 0) return TB_OK;
-  embed_kernel<<<M, 128, 0, st>>>(ids, (const __nv_bfloat16*)emb, ld_emb, d, vocab,
-                                  (const __nv_bfloat16*)g, h, ld_h, (__nv_bfloat16*)hg, ld_hg, sq);
-  return host_err(cudaGetLastError(), "embed launch");
+  return launch_pdl(embed_kernel, dim3(M), dim3(128), 0, st, 1, "embed launch", ids,
+                    (const __nv_bfloat16*)emb, ld_emb, d, vocab, (const __nv_bfloat16*)g, h, ld_h,
+                    (__nv_bfloat16*)hg, ld_hg, sq);
 }
 
 int argmax_launch(const float* logits, int ld, int M, int N, int* out, cudaStream_t st) {
   if (M < 0 || N <= 0 || ld < N) return arg_err("argmax shapes");
   if (M == 0) return TB_OK;
-  argmax_kernel<<<M, 512, 0, st>>>(logits, ld, N, out);
-  return host_err(cudaGetLastError(), "argmax launch");
+  return launch_pdl(argmax_kernel, dim3(M), dim3(512), 0, st, 1, "argmax launch", logits, ld, N,
+                    out);
 }
 
 }  // namespace tb

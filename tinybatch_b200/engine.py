@@ -31,7 +31,7 @@ from .block_manager import BlockManager
 from .config import EngineConfig
 from .kv_cache import PagedKVCache
 from .model import Qwen2Paged
-from .runtime import StepMeta
+from .runtime import DecodeGraph, StepMeta
 from .scheduler import Request, Scheduler
 
 
@@ -46,8 +46,12 @@ class StepOutput:
 
 class LLMEngine:
     def __init__(self, config: EngineConfig | None = None, model: Qwen2Paged | None = None,
-                 tokenizer=None):
+                 tokenizer=None, cuda_graphs: bool = True):
         self.cfg = config or EngineConfig()
+        # decode-only greedy steps replay a CUDA graph captured per batch size
+        self.cuda_graphs = cuda_graphs
+        self._graphs: dict[int, DecodeGraph] = {}
+        self._bt_width = -(-self.cfg.max_model_len // self.cfg.block_size) + 1
         self.device = torch.device(self.cfg.device)
         if model is None:
             model = Qwen2Paged(self.cfg.model_id, self.device, torch.bfloat16)
@@ -145,9 +149,17 @@ class LLMEngine:
             return []
         ordered = batch.prefill + batch.decode
         ids, pos, slices, tables, ctx = self.build_batch(batch)
-        md = self.model.metadata(ids, pos, slices, tables, ctx, self.cfg.block_size)
         greedy = all(r.temperature <= 0.0 for r in ordered)
-        logits = self.model.forward_meta(md, self.kv_cache, sample=greedy)
+        if self.cuda_graphs and greedy and not batch.prefill:
+            g = self.decode_graph(len(ordered))
+            md = StepMeta(ids, pos, slices, tables, ctx, self.cfg.block_size,
+                          self.model.cfg.n_heads // self.model.cfg.n_kv_heads, self.device,
+                          bt_width=self._bt_width, dest=g.dest)
+            g.run(md)
+            logits = self.model.dm.logits[: len(ordered)]
+        else:
+            md = self.model.metadata(ids, pos, slices, tables, ctx, self.cfg.block_size)
+            logits = self.model.forward_meta(md, self.kv_cache, sample=greedy)
         if greedy:
             next_ids = self.model.dm.next_ids[: len(ordered)].cpu().tolist()
             self.last_d2h_bytes = 4 * len(ordered)
@@ -172,6 +184,15 @@ class LLMEngine:
                 self.scheduler.finish(req)
             outputs.append(StepOutput(req.req_id, tok, delta, finished, req))
         return outputs
+
+    def decode_graph(self, n: int) -> DecodeGraph:
+        """The captured decode step for ``n`` sequences (captured on first use)."""
+        g = self._graphs.get(n)
+        if g is None or g.stale():
+            g = DecodeGraph(self.model.dm, self.kv_cache.pools, n, self._bt_width,
+                            self.cfg.max_model_len, self.cfg.block_size)
+            self._graphs[n] = g
+        return g
 
     def _sample(self, logits: torch.Tensor, reqs: list[Request]) -> list[int]:
         """Per-row sampling for non-greedy requests (``src/tinybatch/engine.py:145-159``)."""

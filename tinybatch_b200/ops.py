@@ -20,13 +20,28 @@ class Scratch:
     def __init__(self, device, nbytes: int = 0):
         self.device = torch.device(device)
         self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+        self.version = 0        # bumped on every growth (captured graphs must check it)
+        self._retired: list[torch.Tensor] = []
 
     def get(self, nbytes: int) -> tuple[int | None, int]:
         if nbytes == 0:
             return None, 0
         if nbytes > self.buf.numel():
+            # the old buffer stays alive: a graph captured on it never reads freed memory
+            self._retired.append(self.buf)
             self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self.version += 1
         return self.buf.data_ptr(), self.buf.numel()
+
+
+def _gemm_scratch(scratch: Scratch | None, device, M, n_cols, bn, splits, split_mode):
+    """Scratch for a GEMM call: none for cluster split-K (the default),
+    caller scratch for ``split_mode="global"``."""
+    if splits <= 1 or split_mode == "cluster":
+        return None, 0, None
+    if split_mode != "global":
+        raise ValueError(f"split_mode must be 'cluster' or 'global', not {split_mode!r}")
+    return _scratch(scratch, device, N.load().tb_gemm_scratch_bytes(M, n_cols, bn, splits))
 
 
 def _scratch(scratch: Scratch | None, device, nbytes: int):
@@ -45,11 +60,12 @@ def _sq(sq):
     return ptr(sq), sq.shape[0], sq.stride(0)
 
 
-def linear(x, w, out, *, sq=None, inv_d=0.0, eps=0.0, bn=128, splits=1, scratch=None):
+def linear(x, w, out, *, sq=None, inv_d=0.0, eps=0.0, bn=128, splits=1, scratch=None,
+           split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w.shape[0]
-    ws, wsn, _ = _scratch(scratch, x.device, lib.tb_gemm_scratch_bytes(M, Nn, bn, splits))
+    ws, wsn, _ = _gemm_scratch(scratch, x.device, M, Nn, bn, splits, split_mode)
     sp, parts, sld = _sq(sq)
     N.check(lib.tb_linear(ptr(x), x.stride(0), ptr(w), w.stride(0), M, Nn, K, sp, parts, sld,
                           inv_d, eps, ptr(out), out.stride(0), int(out.dtype == torch.float32),
@@ -59,11 +75,11 @@ def linear(x, w, out, *, sq=None, inv_d=0.0, eps=0.0, bn=128, splits=1, scratch=
 
 def qkv_rope_kv(x, w_qkv, bias, *, n_q_heads, n_kv_heads, head_dim, sq, inv_d, eps,
                 rope_cos, rope_sin, positions, slots, q_out, kv_pool, block_size,
-                bn=128, splits=1, scratch=None):
+                bn=128, splits=1, scratch=None, split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w_qkv.shape[0]
-    ws, wsn, _ = _scratch(scratch, x.device, lib.tb_gemm_scratch_bytes(M, Nn, bn, splits))
+    ws, wsn, _ = _gemm_scratch(scratch, x.device, M, Nn, bn, splits, split_mode)
     sp, parts, sld = _sq(sq)
     N.check(lib.tb_qkv_rope_kv(ptr(x), x.stride(0), ptr(w_qkv), w_qkv.stride(0), ptr(bias), M,
                                K, n_q_heads, n_kv_heads, head_dim, sp, parts, sld, inv_d, eps,
@@ -73,11 +89,12 @@ def qkv_rope_kv(x, w_qkv, bias, *, n_q_heads, n_kv_heads, head_dim, sq, inv_d, e
             "tb_qkv_rope_kv")
 
 
-def gate_up_swiglu(x, w_gu, act, *, n_feat, sq, inv_d, eps, bn=128, splits=1, scratch=None):
+def gate_up_swiglu(x, w_gu, act, *, n_feat, sq, inv_d, eps, bn=128, splits=1, scratch=None,
+                   split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w_gu.shape[0]
-    ws, wsn, _ = _scratch(scratch, x.device, lib.tb_gemm_scratch_bytes(M, Nn, bn, splits))
+    ws, wsn, _ = _gemm_scratch(scratch, x.device, M, Nn, bn, splits, split_mode)
     sp, parts, sld = _sq(sq)
     N.check(lib.tb_gate_up_swiglu(ptr(x), x.stride(0), ptr(w_gu), w_gu.stride(0), M, K, n_feat,
                                   sp, parts, sld, inv_d, eps, ptr(act), act.stride(0), bn,
@@ -86,11 +103,11 @@ def gate_up_swiglu(x, w_gu, act, *, n_feat, sq, inv_d, eps, bn=128, splits=1, sc
 
 
 def row_linear_residual(x, w, h, g_next, hg, sq_out, *, row_dst=None, hg2=None, sq2=None,
-                        bn=128, splits=1, scratch=None):
+                        bn=128, splits=1, scratch=None, split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w.shape[0]
-    ws, wsn, _ = _scratch(scratch, x.device, lib.tb_gemm_scratch_bytes(M, Nn, bn, splits))
+    ws, wsn, _ = _gemm_scratch(scratch, x.device, M, Nn, bn, splits, split_mode)
     N.check(lib.tb_row_linear_residual(
         ptr(x), x.stride(0), ptr(w), w.stride(0), M, Nn, K, ptr(h), h.stride(0), ptr(g_next),
         ptr(hg), hg.stride(0), ptr(sq_out), sq_out.stride(0), ptr(row_dst), ptr(hg2),
@@ -137,3 +154,11 @@ def argmax(logits, out):
     N.check(lib.tb_argmax(ptr(logits), logits.stride(0), M, V, ptr(out), N.stream_ptr()),
             "tb_argmax")
     return out
+
+
+def max_active_clusters(bn: int, cluster: int) -> int:
+    import ctypes
+    out = ctypes.c_int(0)
+    N.check(N.load().tb_gemm_max_active_clusters(bn, cluster, ctypes.byref(out)),
+            "tb_gemm_max_active_clusters")
+    return out.value

@@ -33,27 +33,53 @@ SMS = 148
 
 # ------------------------------------------------------------------ planning
 
-def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 256), max_splits: int = 16) -> tuple[int, int]:
-    """Tile width and split-K factor for a C[M,N] = A[M,K] B[N,K]^T launch.
+_CLUSTERS: list[int] | None = None
+# clusters of 1..8 GEMM CTAs resident at once on a B200 (one CTA per SM);
+# replaced by the device's own answer on first use
+_CLUSTERS_B200 = [148, 74, 45, 33, 26, 22, 15, 15]
 
-    Cost model (arbitrary units): a CTA streams (bn + 32) * k_iters bf16 rows
-    of 64 (B tile plus the share of the A tile that misses L2), pays a fixed
-    setup cost, and a split pays its fp32 partial round trip; the launch
-    takes ceil(CTAs / 148) such waves."""
+
+def _cluster_capacity() -> list[int]:
+    global _CLUSTERS
+    if _CLUSTERS is None:
+        try:
+            _CLUSTERS = [ops.max_active_clusters(128, c) for c in range(1, 9)]
+        except Exception:
+            _CLUSTERS = list(_CLUSTERS_B200)
+    return _CLUSTERS
+
+
+def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int = 8) -> tuple[int, int]:
+    """Tile width and cluster split-K factor for C[M,N] = A[M,K] B[N,K]^T.
+
+    Time model (fitted to B200 measurements of the decode shapes): a CTA
+    streams its B slice plus ~35% of its A slice (the rest hits L2) at
+    min(50 GB/s, 6 TB/s / active CTAs) or is bound by its share of the
+    tensor pipe (~10.8 TFLOP/s per SM); ~1 us of epilogue and 0.25 us per
+    extra cluster member for the DSMEM reduction.  A launch with more CTAs
+    than fit at once runs (CTAs / resident CTAs) waves of fully busy SMs."""
+    cap = _cluster_capacity()
     tm = -(-M // 128)
     num_k = -(-K // 64)
     best = None
     for bn in bns:
         tiles = tm * -(-N // bn)
         for s in range(1, max_splits + 1):
-            if s > num_k or (s > 1 and num_k / s < 4):
+            if s > num_k or (s > 1 and num_k / s < 2):
                 break
             ctas = tiles * s
-            waves = -(-ctas // SMS)
-            per_cta = -(-num_k // s) * (bn + 32) + 160 + (bn if s > 1 else 0)
-            cost = waves * per_cta
-            if best is None or cost < best[0]:
-                best = (cost, bn, s)
+            k_it = -(-num_k // s)
+            cta_bytes = k_it * 64 * 2 * (bn + 0.35 * 128)
+            cta_flops = 2.0 * 128 * bn * 64 * k_it
+            fixed = 1e-6 + 0.25e-6 * (s - 1)
+            if tiles <= cap[s - 1]:
+                bw = min(50e9, 6.0e12 / ctas)
+                t = max(cta_bytes / bw, cta_flops / 10.8e12) + fixed
+            else:     # several waves of fully busy SMs (39 GB/s each)
+                waves = ctas / (cap[s - 1] * s)
+                t = waves * (max(cta_bytes / 39e9, cta_flops / 10.8e12) + fixed)
+            if best is None or t < best[0]:
+                best = (t, bn, s)
     return best[1], best[2]
 
 
@@ -90,7 +116,9 @@ class RankWeights:
     on the rank's device.  ``w`` is the full (unsharded) HF-named dict; the
     split is the Megatron one of ``src/tinybatch/tensor_parallel.py:35-61``."""
 
-    GU_BN = 128
+    # gate/up tile: 96 features of gate + 96 of up; 13824/t features give
+    # 144 tiles at t = 1, 72 at t = 2 ... so decode fills ~144 SMs at any degree
+    GU_BN = 192
 
     def __init__(self, cfg: ModelConfig, w: dict, rank: int = 0, world: int = 1,
                  device="cuda", sharded: bool = False):
@@ -162,7 +190,12 @@ class StepMeta:
 
     def __init__(self, token_ids, positions, seq_slices, block_tables, context_lens,
                  block_size: int, group: int, device, pinned: bool = True,
-                 all_logits: bool = False):
+                 all_logits: bool = False, bt_width: int = 0,
+                 dest: torch.Tensor | None = None):
+        """``bt_width`` pads the block tables to at least that many columns
+        (a fixed layout for CUDA-graph replay); ``dest``, a device int32
+        buffer of exactly the packed size, receives the metadata instead of
+        a fresh allocation."""
         if isinstance(token_ids, torch.Tensor):
             token_ids = token_ids.detach().cpu().numpy()
         if isinstance(positions, torch.Tensor):
@@ -194,7 +227,7 @@ class StepMeta:
 
         def subset(mask):
             idx = np.nonzero(mask)[0]
-            bt_ld = max([len(block_tables[i]) for i in idx], default=1) or 1
+            bt_ld = max([len(block_tables[i]) for i in idx] + [bt_width, 1])
             bt = np.full((len(idx), bt_ld), -1, dtype=np.int32)
             for r, i in enumerate(idx):
                 bt[r, :len(block_tables[i])] = block_tables[i]
@@ -210,7 +243,16 @@ class StepMeta:
         host = torch.from_numpy(flat)
         if pinned and torch.device(device).type == "cuda":
             host = host.pin_memory()
-        buf = host.to(device, non_blocking=True)
+        if dest is not None:
+            if dest.numel() != flat.size:
+                raise ValueError("metadata layout differs from the destination buffer")
+            dest.copy_(host, non_blocking=True)
+            buf = dest
+        else:
+            buf = host.to(device, non_blocking=True)
+        self.buf = buf
+        self.layout = (T, n, int(is_dec.sum()), d_bt.shape[1], p_bt.shape[1], work.shape[0],
+                       all_logits)
         self.h2d_bytes = flat.nbytes
         views, o = [], 0
         for a in parts:
@@ -265,8 +307,18 @@ class DeviceModel:
         self.prof.append((kind, s, e, nbytes, flops))
         return r
 
+    def generation(self) -> tuple:
+        """Changes whenever a buffer a captured graph may point to is replaced."""
+        return (self._alloc_gen, self.scratch.version, self.attn_scratch.version)
+
     def _alloc(self, T: int, S: int) -> None:
         cfg, w, dev = self.cfg, self.w, self.device
+        self._alloc_gen = getattr(self, "_alloc_gen", -1) + 1
+        # previous buffers stay referenced so a stale graph cannot touch freed memory
+        self._retired = getattr(self, "_retired", [])
+        if hasattr(self, "h"):
+            self._retired.append((self.h, self.hg, self.sq, self.q, self.attn, self.act,
+                                  self.hg_last, self.sq_last, self.logits, self.next_ids))
         d = cfg.d_model
         self.T_max, self.S_max = T, S
         self.parts_max = max(-(-d // 64), 1)
@@ -301,7 +353,10 @@ class DeviceModel:
         return -(-Nn // bn)
 
     def forward(self, md: StepMeta, kv_pools: list[torch.Tensor], compute_logits: bool = True,
-                sample: bool = False):
+                sample: bool = False, attn_max_ctx: int | None = None):
+        """Launch the forward.  ``attn_max_ctx`` sizes the decode attention
+        grid (default: this batch's longest context); a CUDA graph passes its
+        bound so one capture serves every context length up to it."""
         cfg, W = self.cfg, self.w
         T, n = md.T, md.n_out
         self.ensure(T, n)
@@ -316,7 +371,8 @@ class DeviceModel:
         parts = 1
         for li, L in enumerate(W.layers):
             pool = kv_pools[li]
-            bn, splits = plan_gemm(T, L.wqkv.shape[0], d, bns=(128, 256) if hd > 64 else (64, 128, 256))
+            bns = tuple(b for b in (64, 128, 192, 256) if b % hd == 0)
+            bn, splits = plan_gemm(T, L.wqkv.shape[0], d, bns=bns)
             Nq = L.wqkv.shape[0]
             self._run("qkv_rope_kv", 2 * Nq * d + 2 * T * d + 2 * T * Nq, 2.0 * T * Nq * d,
                       ops.qkv_rope_kv, self.hg[:T], L.wqkv, L.bqkv, n_q_heads=W.n_q, n_kv_heads=W.n_kv,
@@ -331,7 +387,8 @@ class DeviceModel:
                     "attention_decode", dec_ctx * kv_row + 2 * md.dec_tokens * qrow,
                     4.0 * md.dec_ctx_sum * W.n_q * hd, ops.paged_attention_decode,
                     self.q, self.attn, pool, block_tables=md.dec_bt, q_start=md.dec_q_start,
-                    q_len=md.dec_q_len, ctx_len=md.dec_ctx, max_ctx=md.dec_max_ctx,
+                    q_len=md.dec_q_len, ctx_len=md.dec_ctx,
+                    max_ctx=attn_max_ctx or md.dec_max_ctx,
                     split_tokens=self.split_tokens, scratch=self.attn_scratch, **akw)
             if md.n_pre:
                 self._run(
@@ -361,3 +418,54 @@ class DeviceModel:
         if sample:
             self._run("argmax", 4 * n * V, 0.0, ops.argmax, out, self.next_ids[:n])
         return out
+
+
+class DecodeGraph:
+    """One decode step of ``n`` sequences captured as a CUDA graph.
+
+    The graph reads its metadata from a static device buffer laid out for
+    ``n`` decode sequences with block tables ``bt_width`` wide; attention is
+    sized for contexts up to ``max_ctx``.  ``run(md)`` expects ``md`` built
+    into ``self.dest`` (``StepMeta(..., bt_width=, dest=graph.dest)``), or
+    copies it there, then replays: every kernel of the step, no host work."""
+
+    def __init__(self, dm: DeviceModel, kv_pools, n: int, bt_width: int, max_ctx: int,
+                 block_size: int):
+        self.dm, self.pools = dm, kv_pools
+        self.n, self.bt_width, self.max_ctx = n, bt_width, max_ctx
+        group = dm.cfg.n_heads // dm.cfg.n_kv_heads
+        # a valid dummy batch: every sequence has one token at position 0 in block 0
+        self.md = StepMeta([0] * n, [0] * n, [(i, i + 1) for i in range(n)],
+                           [[0]] * n, [1] * n, block_size, group, dm.device,
+                           bt_width=bt_width)
+        self.dest = self.md.buf
+        # one eager run (sizes the scratch arenas and sets kernel attributes
+        # outside the capture) on a throw-away one-block pool per layer, so the
+        # dummy batch never writes into the live cache; the capture itself
+        # executes nothing and records the real pools
+        p0 = kv_pools[0]
+        dummy = [torch.zeros((1,) + tuple(p0.shape[1:]), dtype=p0.dtype, device=p0.device)
+                 for _ in kv_pools]
+        dm.forward(self.md, dummy, sample=True, attn_max_ctx=max_ctx)
+        torch.cuda.synchronize(dm.device)
+        del dummy
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            dm.forward(self.md, kv_pools, sample=True, attn_max_ctx=max_ctx)
+        torch.cuda.synchronize(dm.device)
+        self.gen = dm.generation()
+
+    def stale(self) -> bool:
+        return self.gen != self.dm.generation()
+
+    def matches(self, md: StepMeta) -> bool:
+        return md.layout == self.md.layout and md.dec_max_ctx <= self.max_ctx
+
+    def run(self, md: StepMeta) -> None:
+        if self.stale():
+            raise RuntimeError("decode graph is stale: a buffer it uses was reallocated")
+        if md.buf.data_ptr() != self.dest.data_ptr():
+            if not self.matches(md):
+                raise ValueError("batch does not fit the captured decode graph")
+            self.dest.copy_(md.buf)
+        self.graph.replay()
