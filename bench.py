@@ -229,7 +229,7 @@ def run_ours(args) -> None:
     comm = None
     if world > 1:
         from tinybatch_b200.comm import TPComm
-        comm = TPComm.from_process_group(dev)
+        comm = TPComm.from_process_group(dev, n_cols=cfg.d_model, max_rows=args.max_batch_tokens)
 
     w = synthetic_weights(cfg, SEED, dtype=torch.bfloat16, device=dev)
     model = Qwen2Paged.from_weights(cfg, w, device=dev, rank=rank, world=world, comm=comm,

@@ -46,6 +46,15 @@ extern "C" {
 int tb_version(void);
 const char* tb_last_error(void);
 
+/* Debug timeline: while buf is not NULL, every GEMM launched afterwards by
+ * this process writes, per CTA c, %globaltimer stamps (ns) to buf[16*c + k]
+ * for k = 0 start, 1 loads issued, 2 accumulator ready, 3 partials pushed,
+ * 4 partners seen, 5 sums delivered, 6 end, 7 partial parked, 8 cluster
+ * synced, 9 epilogue body done, 10 row sums combined (unreached points are
+ * left as they were).  buf must hold 16 entries per CTA of the largest
+ * launch.  Not thread-safe; NULL turns it off. */
+int tb_debug_trace(unsigned long long* buf);
+
 /* Read (and optionally clear) the device status word of the current device.
  * Synchronises the device. */
 int tb_status(unsigned int* code_h, int clear);
@@ -154,6 +163,41 @@ int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M
                            float* sq_out, int sq_out_ld, const int* row_dst, void* hg2,
                            float* sq2, int sq2_ld, int bn, int splits, void* ws,
                            size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------- tensor-parallel comm
+ * One communicator per rank (one process per GPU).  It owns one device
+ * allocation per rank (exchange buffers for max_rows x n_cols bf16 partials,
+ * delivery flags for max_ctas CTAs, a step counter), made at creation and
+ * shared with the other ranks through CUDA IPC:
+ *   1. tb_comm_create on every rank -> a 64-byte cudaIpcMemHandle;
+ *   2. exchange the handles (e.g. torch.distributed all_gather);
+ *   3. tb_comm_open with all world handles in rank order;
+ *   4. per forward: tb_comm_begin_step, then the row-parallel projections
+ *      with site = 0, 1, ... n_sites-1 in the same order on every rank;
+ *   5. after a barrier, tb_comm_destroy.
+ * Replaces torch.distributed all_reduce(SUM) in the reference's
+ * tensor_parallel.py:76-84 (called at :108 and :114). */
+int tb_comm_create(int rank, int world, int max_rows, int n_cols, int max_ctas, void** comm_out,
+                   void* ipc_handle_out);
+int tb_comm_open(void* comm, const void* ipc_handles);
+int tb_comm_begin_step(void* comm, void* stream);
+int tb_comm_destroy(void* comm);
+
+/* Row-parallel projection with the all-reduce fused into its epilogue:
+ *   h += sum over ranks of (x_r . w_r^T)   (x_r, w_r: this rank's K shard)
+ * then hg / sq_out as tb_row_linear_residual.  Each CTA pushes its bf16
+ * partial tile to the peers over NVLink (two_shot = 0: to every rank, which
+ * sums the partials in rank order; two_shot = 1: to the column's owner, which
+ * sums and broadcasts), so h stays identical on all ranks.  Every rank must
+ * make the same calls (same M, N, K, bn, splits, site) in the same order.
+ * A partner that does not arrive within 5 s sets TB_STATUS_PEER_TIMEOUT.
+ * Replaces allreduce(F.linear(attn, Wo)) / allreduce(F.linear(act, Wd)) + the
+ * residual add and next _rms_norm (tensor_parallel.py:108-110, :114-116). */
+int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int ldw, int M, int N,
+                                     int K, float* h, int ld_h, const void* g_next, void* hg,
+                                     int ld_hg, float* sq_out, int sq_out_ld, const int* row_dst,
+                                     void* hg2, float* sq2, int sq2_ld, void* comm, int site,
+                                     int n_sites, int two_shot, int bn, int splits, void* stream);
 
 /* ------------------------------------------------------------- attention
  * Paged GQA attention reading K/V through block tables (no gather copy).

@@ -23,6 +23,7 @@ STATUS_NAMES = {101: "pipeline barrier wait ran out", 102: "peer flag wait ran o
 _SIGS = {
     "tb_version": (c_int, []),
     "tb_last_error": (ctypes.c_char_p, []),
+    "tb_debug_trace": (c_int, [c_void_p]),
     "tb_status": (c_int, [ctypes.POINTER(c_uint), c_int]),
     "tb_gemm_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "tb_gemm_max_active_clusters": (c_int, [c_int, c_int, ctypes.POINTER(c_int)]),
@@ -50,6 +51,16 @@ _SIGS = {
                                            c_int, c_int, c_int, c_int, c_void_p, c_int,
                                            c_void_p, c_void_p, c_void_p, c_int,
                                            c_void_p, c_int, c_void_p]),
+    "tb_comm_create": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p),
+                               c_void_p]),
+    "tb_comm_open": (c_int, [c_void_p, c_void_p]),
+    "tb_comm_begin_step": (c_int, [c_void_p, c_void_p]),
+    "tb_comm_destroy": (c_int, [c_void_p]),
+    "tb_row_linear_allreduce_residual": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int,
+                                                 c_int, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                                                 c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                                 c_int, c_void_p, c_int, c_int, c_int, c_int,
+                                                 c_int, c_void_p]),
     "tb_embed": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p,
                          c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "tb_argmax": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),

@@ -5,6 +5,7 @@
 #include "host.h"
 
 namespace tb {
+extern unsigned long long* g_debug_trace;
 const char* last_error();
 int embed_launch(const int* ids, int M, const void* emb, int ld_emb, int d, int vocab,
                  const void* g, float* h, int ld_h, void* hg, int ld_hg, float* sq,
@@ -68,6 +69,11 @@ bool valid_bn(int bn) { return bn == 64 || bn == 128 || bn == 192 || bn == 256; 
 extern "C" {
 
 int tb_version(void) { return 1; }
+
+int tb_debug_trace(unsigned long long* buf) {
+  g_debug_trace = buf;
+  return TB_OK;
+}
 
 const char* tb_last_error(void) { return last_error(); }
 

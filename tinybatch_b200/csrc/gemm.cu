@@ -20,6 +20,11 @@ enum SplitMode : int {
                       // reduces a slice of columns over DSMEM
 };
 
+__device__ __forceinline__ void trace_at(const GemmArgs& g, int point) {
+  if (g.trace != nullptr)
+    g.trace[(size_t)(blockIdx.x + blockIdx.y * gridDim.x) * TR_POINTS + point] = globaltimer_ns();
+}
+
 constexpr int tmem_cols(int bn) { return bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256; }
 
 template <int BN, int STAGES>
@@ -81,17 +86,27 @@ struct AccReader {
   template <int W>
   __device__ __forceinline__ void load(int c, float* v) const {
     if (mode == SPLIT_CLUSTER) {
+      // ordered sum over the cluster members, the next member's loads in
+      // flight while the current one is added
+      const uint32_t off = (uint32_t)(((c / 4) * BM + row) * 16);
+      float4 cur[W / 4], nxt[W / 4];
+#pragma unroll
+      for (int i = 0; i < W / 4; ++i) cur[i] = ld_cluster_v4(cluster_map(red, 0) + off + i * BM * 16);
 #pragma unroll
       for (int j = 0; j < W; ++j) v[j] = 0.f;
       for (int s = 0; s < splits; ++s) {
-        const uint32_t base = cluster_map(red, s);
+        if (s + 1 < splits) {
+          const uint32_t base = cluster_map(red, s + 1) + off;
+#pragma unroll
+          for (int i = 0; i < W / 4; ++i) nxt[i] = ld_cluster_v4(base + i * BM * 16);
+        }
 #pragma unroll
         for (int i = 0; i < W / 4; ++i) {
-          const float4 x = ld_cluster_v4(base + (uint32_t)(((c / 4 + i) * BM + row) * 16));
-          v[4 * i] += x.x;
-          v[4 * i + 1] += x.y;
-          v[4 * i + 2] += x.z;
-          v[4 * i + 3] += x.w;
+          v[4 * i] += cur[i].x;
+          v[4 * i + 1] += cur[i].y;
+          v[4 * i + 2] += cur[i].z;
+          v[4 * i + 3] += cur[i].w;
+          cur[i] = nxt[i];
         }
       }
       return;
@@ -121,13 +136,287 @@ struct AccReader {
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Residual inputs of the first PF 16-column units this thread updates (its row
+// of h and the next norm's weight), loaded by the epilogue warps before they
+// wait for the accumulator: they do not depend on it, so their latency hides
+// under the main loop.
+constexpr int PF = 3;
+struct ResidPre {
+  float h[PF][16];
+  uint32_t g[PF][8];  // bf16 pairs
+};
+
+__device__ __forceinline__ void load_resid_inputs(const GemmArgs& g, int m, int n, float* h16,
+                                                  uint32_t* g8) {
+  const float4* hp = reinterpret_cast<const float4*>(g.h + (size_t)m * g.ld_h + n);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 x = hp[i];
+    h16[4 * i] = x.x;
+    h16[4 * i + 1] = x.y;
+    h16[4 * i + 2] = x.z;
+    h16[4 * i + 3] = x.w;
+  }
+  const uint4 a = *reinterpret_cast<const uint4*>(g.gnext + n);
+  const uint4 b = *reinterpret_cast<const uint4*>(g.gnext + n + 8);
+  g8[0] = a.x; g8[1] = a.y; g8[2] = a.z; g8[3] = a.w;
+  g8[4] = b.x; g8[5] = b.y; g8[6] = b.z; g8[7] = b.w;
+}
+
+template <int BN>
+__device__ __forceinline__ void resid_prefetch(const GemmArgs& g, int tm, int tn, int row,
+                                               int own, int n_own, ResidPre& p) {
+  const int m = tm * BM + row;
+  if (m >= g.M) return;
+#pragma unroll
+  for (int k = 0; k < PF; ++k) {
+    const int u = own + k * n_own;
+    const int n = tn * BN + u * 16;
+    if (u < BN / 16 && n < g.N) load_resid_inputs(g, m, n, p.h[k], p.g[k]);
+  }
+}
+
+// h = h_old + v (h_old, g given), hg = bf16(h * g) (and its copy in hg2 row
+// dst if dst >= 0); returns the sum of the new h^2 over the 16 columns.
+__device__ __forceinline__ float resid_update(const GemmArgs& g, int m, int n, int dst,
+                                              const float* v, const float* h_old,
+                                              const uint32_t* g8) {
+  float hn[16], o[16], ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) hn[j] = h_old[j] + v[j];
+  float4* hp = reinterpret_cast<float4*>(g.h + (size_t)m * g.ld_h + n);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hp[i] = make_float4(hn[4 * i], hn[4 * i + 1], hn[4 * i + 2], hn[4 * i + 3]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    __nv_bfloat162 w2 = *reinterpret_cast<const __nv_bfloat162*>(&g8[i]);
+    const float2 wf = __bfloat1622float2(w2);
+    o[2 * i] = hn[2 * i] * wf.x;
+    o[2 * i + 1] = hn[2 * i + 1] * wf.y;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) ss += hn[j] * hn[j];
+  __nv_bfloat16* hgp = g.hg + (size_t)m * g.ld_hg + n;
+  store_bf16x8(hgp, o);
+  store_bf16x8(hgp + 8, o + 8);
+  if (dst >= 0) {
+    __nv_bfloat16* p2 = g.hg2 + (size_t)dst * g.ld_hg + n;
+    store_bf16x8(p2, o);
+    store_bf16x8(p2 + 8, o + 8);
+  }
+  return ss;
+}
+
+// Runs `body(k, u, n, h_old, g8)` for every 16-column unit this thread
+// updates: units own, own + n_own, ... of the tile below N; the first PF take
+// their residual inputs from the prefetch, later ones load them on the spot.
+// `body` may contain warp-collective accumulator reads: the unit loop is
+// uniform across the warp.
+template <int BN, class Body>
+__device__ __forceinline__ void for_resid_units(const GemmArgs& g, int m, int tn, int own,
+                                                int n_own, const ResidPre& pre, Body body) {
+  constexpr int U = BN / 16;
+  const bool valid = m < g.M;
+#pragma unroll
+  for (int k = 0; k < PF; ++k) {
+    const int u = own + k * n_own;
+    const int n = tn * BN + u * 16;
+    if (u < U && n < g.N) body(u, n, pre.h[k], pre.g[k]);
+  }
+  for (int u = own + PF * n_own; u < U; u += n_own) {
+    const int n = tn * BN + u * 16;
+    if (n >= g.N) break;
+    float h16[16];
+    uint32_t g8[8];
+    if (valid) load_resid_inputs(g, m, n, h16, g8);
+    body(u, n, h16, g8);
+  }
+}
+
+// 8 bf16 values as fp32, read around L1 (they were written by other GPUs).
+__device__ __forceinline__ void ld_bf16x8_cg(const __nv_bfloat16* p, float* v) {
+  const uint4 a = __ldcg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __bfloat1622float2(pa[i]);
+    v[2 * i] = x.x;
+    v[2 * i + 1] = x.y;
+  }
+}
+
+__device__ __forceinline__ void pack_bf16x16(const float* v, uint4& lo, uint4& hi) {
+  lo.x = pack_bf16x2(v[0], v[1]);
+  lo.y = pack_bf16x2(v[2], v[3]);
+  lo.z = pack_bf16x2(v[4], v[5]);
+  lo.w = pack_bf16x2(v[6], v[7]);
+  hi.x = pack_bf16x2(v[8], v[9]);
+  hi.y = pack_bf16x2(v[10], v[11]);
+  hi.z = pack_bf16x2(v[12], v[13]);
+  hi.w = pack_bf16x2(v[14], v[15]);
+}
+
+// One system fence (cumulative: it orders the CTA's pushes, which the caller
+// made visible to this thread with a CTA barrier after each thread's own
+// fence), then a relaxed flag store to every rank.
+template <class F>
+__device__ __forceinline__ void signal_peers(const CommDev& c, F flag_of, uint32_t epoch) {
+  fence_sys();
+  for (int p = 0; p < c.world; ++p) st_relaxed_sys(flag_of(p), epoch);
+}
+
+// Row-parallel epilogue with the all-reduce across tensor-parallel ranks
+// fused in (all 128 epilogue threads call it; it synchronises them).
+//
+//   one-shot  every rank pushes its bf16 partial of the CTA's columns to
+//             every rank; each rank sums the world partials in rank order
+//   two-shot  every rank pushes each column's partial to the column's owner
+//             (rank n / (N / world)); the owner sums them in rank order and
+//             pushes the bf16 sum to every rank
+// Every rank then adds the same bf16 values to its replicated fp32 residual,
+// so h stays bit-identical on all ranks.  A CTA's partners are the CTAs
+// with the same index on the other ranks; "delivered" flags carry the call's
+// epoch (release stores after a system fence; acquire loads, bounded wait).
+//
+// Exchange layout: [tile][16-column unit][half][128 rows][8 columns] bf16, the
+// epilogue's own thread order (thread = row), so one warp store or load
+// instruction moves 512 contiguous bytes over NVLink.
+template <int BN>
+__device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader<BN>& acc, int tm,
+                                           int tn, int row, int own, int n_own,
+                                           const ResidPre& pre) {
+  const CommDev& c = g.comm;
+  const int m = tm * BM + row;
+  const bool valid = m < g.M;
+  const int N = g.N;
+  const uint32_t epoch = c.state[0] * (uint32_t)c.n_sites + (uint32_t)c.site + 1u;
+  const int par = (int)(epoch & 1u);
+  // plane: every tile of a max_rows x n_cols output, padded to whole tiles
+  const size_t plane = (size_t)((c.max_rows + BM - 1) / BM) * BM * (size_t)(c.n_cols + 256);
+  const int cta = blockIdx.x;
+  const int per_owner = N / c.world;
+  const bool leader = threadIdx.x == 64;
+  constexpr int U = BN / 16;
+  const size_t tile_base = ((size_t)tm * g.tiles_n + tn) * U;
+  auto xoff = [&](int u, int half) {
+    return (((tile_base + u) * 2 + half) * BM + row) * 8;
+  };
+  auto rs_at = [&](int p, int src) { return c.rs[p] + ((size_t)par * c.world + src) * plane; };
+  auto flag_at = [&](int p, int kind, int src) {
+    return c.flags[p] + ((size_t)((kind * 2 + par) * c.world + src)) * c.max_ctas + cta;
+  };
+  auto put16 = [&](__nv_bfloat16* base, int u, const float* v) {
+    uint4 lo, hi;
+    pack_bf16x16(v, lo, hi);
+    *reinterpret_cast<uint4*>(base + xoff(u, 0)) = lo;
+    *reinterpret_cast<uint4*>(base + xoff(u, 1)) = hi;
+  };
+
+  // 1. push this rank's partials
+  for (int u = own; u < U; u += n_own) {
+    const int n = tn * BN + u * 16;
+    if (n >= N) break;
+    float v[16];
+    acc.template load<16>(u * 16, v);
+    if (!valid) continue;
+    if (c.two_shot) {
+      put16(rs_at(n / per_owner, c.rank), u, v);
+    } else {
+      for (int p = 0; p < c.world; ++p) put16(rs_at(p, c.rank), u, v);
+    }
+  }
+  fence_sys();
+  epi_bar();
+  if (leader) {
+    trace_at(g, TR_PUSHED);
+    signal_peers(c, [&](int p) { return flag_at(p, 0, c.rank); }, epoch);
+    for (int s = 0; s < c.world; ++s) wait_flag_sys(flag_at(c.rank, 0, s), epoch);
+    trace_at(g, TR_PARTNERS);
+  }
+  epi_bar();
+
+  // the world partials of unit u summed in rank order; the next rank's loads
+  // are in flight while the current rank's are added
+  auto sum_partials = [&](int u, float* v) {
+    uint4 cur0, cur1, nxt0, nxt1;
+    cur0 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, 0) + xoff(u, 0)));
+    cur1 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, 0) + xoff(u, 1)));
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+    for (int s = 0; s < c.world; ++s) {
+      if (s + 1 < c.world) {
+        nxt0 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, s + 1) + xoff(u, 0)));
+        nxt1 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, s + 1) + xoff(u, 1)));
+      }
+      const __nv_bfloat162* q0 = reinterpret_cast<const __nv_bfloat162*>(&cur0);
+      const __nv_bfloat162* q1 = reinterpret_cast<const __nv_bfloat162*>(&cur1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __bfloat1622float2(q0[i]);
+        const float2 b = __bfloat1622float2(q1[i]);
+        v[2 * i] += a.x;
+        v[2 * i + 1] += a.y;
+        v[8 + 2 * i] += b.x;
+        v[8 + 2 * i + 1] += b.y;
+      }
+      cur0 = nxt0;
+      cur1 = nxt1;
+    }
+  };
+
+  const int dst = (valid && g.row_dst != nullptr) ? g.row_dst[m] : -1;
+  float ss = 0.f;
+  if (!c.two_shot) {
+    // 2. sum the world partials in rank order and apply
+    for_resid_units<BN>(g, m, tn, own, n_own, pre,
+                        [&](int u, int n, const float* h_old, const uint32_t* g8) {
+                          if (!valid) return;
+                          float v[16];
+                          sum_partials(u, v);
+                          ss += resid_update(g, m, n, dst, v, h_old, g8);
+                        });
+    return ss;
+  }
+
+  // 2'. owners reduce their columns and broadcast the bf16 sums
+  const size_t ag_off = (size_t)par * plane;
+  for (int u = own; u < U; u += n_own) {
+    const int n = tn * BN + u * 16;
+    if (n >= N) break;
+    if (!valid || n / per_owner != c.rank) continue;
+    float v[16];
+    sum_partials(u, v);
+    for (int p = 0; p < c.world; ++p) put16(c.ag[p] + ag_off, u, v);
+  }
+  fence_sys();
+  epi_bar();
+  if (leader) {
+    signal_peers(c, [&](int p) { return flag_at(p, 1, c.rank); }, epoch);
+    for (int s = 0; s < c.world; ++s) wait_flag_sys(flag_at(c.rank, 1, s), epoch);
+    trace_at(g, TR_SUMS);
+  }
+  epi_bar();
+  // 3. every rank applies the same reduced sums
+  for_resid_units<BN>(g, m, tn, own, n_own, pre,
+                      [&](int u, int n, const float* h_old, const uint32_t* g8) {
+                        if (!valid) return;
+                        float v[16];
+                        const __nv_bfloat16* src = c.ag[c.rank] + ag_off;
+                        ld_bf16x8_cg(src + xoff(u, 0), v);
+                        ld_bf16x8_cg(src + xoff(u, 1), v + 8);
+                        ss += resid_update(g, m, n, dst, v, h_old, g8);
+                      });
+  return ss;
+}
+
 // The fused epilogue for this thread's row.  Work is divided in units (a
 // 16-column chunk; a head for EPI_QKV); this CTA handles the units u with
 // u % n_own == own (all units unless the tile is split over a cluster).
 // EPI_RESID returns the row's sum of h^2 over the handled columns.
 template <int BN, int EPI>
 __device__ __forceinline__ float run_epilogue(const GemmArgs& g, const AccReader<BN>& acc, int tm,
-                                              int tn, int row, int own, int n_own) {
+                                              int tn, int row, int own, int n_own,
+                                              const ResidPre& pre) {
   const int m = tm * BM + row;
   const bool valid = m < g.M;
   const float rs = row_scale(g, m);
@@ -185,46 +474,14 @@ __device__ __forceinline__ float run_epilogue(const GemmArgs& g, const AccReader
       store_bf16x8(o + 8, y + 8);
     }
   } else if constexpr (EPI == EPI_RESID) {
+    if (g.comm.world > 1) return run_resid_tp<BN>(g, acc, tm, tn, row, own, n_own, pre);
     const int dst = (valid && g.row_dst != nullptr) ? g.row_dst[m] : -1;
-    for (int u = own; u < BN / 16; u += n_own) {
-      const int c = u * 16;
-      const int n = tn * BN + c;
-      if (n >= g.N) break;
-      float v[16];
-      acc.template load<16>(c, v);
-      if (!valid) continue;
-      float* hp = g.h + (size_t)m * g.ld_h + n;
-      float gw[16], hv[16];
-      load_bf16x8(g.gnext + n, gw);
-      load_bf16x8(g.gnext + n + 8, gw + 8);
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        float4 x = *reinterpret_cast<const float4*>(hp + j);
-        x.x += v[j];
-        x.y += v[j + 1];
-        x.z += v[j + 2];
-        x.w += v[j + 3];
-        *reinterpret_cast<float4*>(hp + j) = x;
-        hv[j] = x.x;
-        hv[j + 1] = x.y;
-        hv[j + 2] = x.z;
-        hv[j + 3] = x.w;
-      }
-      float o[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        ss += hv[j] * hv[j];
-        o[j] = hv[j] * gw[j];
-      }
-      __nv_bfloat16* hgp = g.hg + (size_t)m * g.ld_hg + n;
-      store_bf16x8(hgp, o);
-      store_bf16x8(hgp + 8, o + 8);
-      if (dst >= 0) {
-        __nv_bfloat16* p2 = g.hg2 + (size_t)dst * g.ld_hg + n;
-        store_bf16x8(p2, o);
-        store_bf16x8(p2 + 8, o + 8);
-      }
-    }
+    for_resid_units<BN>(g, m, tn, own, n_own, pre,
+                        [&](int u, int n, const float* h_old, const uint32_t* g8) {
+                          float v[16];
+                          acc.template load<16>(u * 16, v);
+                          if (valid) ss += resid_update(g, m, n, dst, v, h_old, g8);
+                        });
   } else if constexpr (EPI == EPI_QKV) {
     const int hd = g.head_dim, half = hd >> 1;
     const int heads_in_tile = BN / hd;
@@ -358,7 +615,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (threadIdx.x == 0) pdl_trigger();
+  if (threadIdx.x == 0) {
+    pdl_trigger();
+    trace_at(g, TR_START);
+  }
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer
@@ -379,6 +639,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tma_load_2d(sA + s * A_BYTES, &tma_a, &full[s], it * BK, tm * BM);
       tma_load_2d(sB + s * L::B_BYTES, &tma_b, &full[s], it * BK, tn * BN);
     }
+    trace_at(g, TR_LOADS_ISSUED);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
     constexpr uint32_t idesc = idesc_bf16_m128(BN);
@@ -413,7 +674,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   acc.ws = nullptr;
   acc.red = smem_u32(smem);
 
-  if (warp >= 2) pdl_wait();   // the epilogue reads and writes buffers earlier kernels use
+  ResidPre pre;
+  if (warp >= 2) {
+    pdl_wait();   // the epilogue reads and writes buffers earlier kernels use
+    if constexpr (EPI == EPI_RESID) {
+      if (mode == SPLIT_CLUSTER) resid_prefetch<BN>(g, tm, tn, row, z, g.splits, pre);
+      else resid_prefetch<BN>(g, tm, tn, row, 0, 1, pre);
+    }
+  }
   if (mode == SPLIT_CLUSTER) {
     // 1. park this CTA's fp32 partial over its (idle) stage ring as
     //    float4 [BN/4][BM]; every MMA and TMA write has completed once
@@ -421,6 +689,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (warp >= 2) {
       mbar_wait(done, 0);
       tc_fence_after();
+      if (threadIdx.x == 64) trace_at(g, TR_ACC_READY);
       float4* red = reinterpret_cast<float4*>(smem);
       for (int c = 0; c < BN; c += 16) {
         float v[16];
@@ -429,15 +698,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int i = 0; i < 4; ++i)
           red[(c / 4 + i) * BM + row] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
+      if (threadIdx.x == 64) trace_at(g, TR_PARKED);
     }
     cluster_sync_all();
+    if (threadIdx.x == 64) trace_at(g, TR_CLUSTER_SYNC);
     // 2. reduce this CTA's share of the columns across the cluster and run
     //    the epilogue on it
     float ss = 0.f;
-    if (warp >= 2) ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, z, g.splits);
+    if (warp >= 2) ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, z, g.splits, pre);
     if constexpr (EPI == EPI_RESID) {
       if (warp >= 2) row_ss[row] = ss;
     }
+    if (threadIdx.x == 64) trace_at(g, TR_BODY);
     cluster_sync_all();
     // 3. rank 0 of the cluster combines the per-row sums of h^2
     if constexpr (EPI == EPI_RESID) {
@@ -448,10 +720,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         store_row_sumsq(g, tm, tn, row, tot);
       }
     }
+    if (threadIdx.x == 64) trace_at(g, TR_COMBINED);
     cluster_sync_all();
+    if (threadIdx.x == 64) trace_at(g, TR_END);
   } else if (warp >= 2) {
     mbar_wait(done, 0);
     tc_fence_after();
+    if (threadIdx.x == 64) trace_at(g, TR_ACC_READY);
     bool run = true;
     if (mode == SPLIT_GLOBAL) {
       const size_t tile_lin = (size_t)tm * g.tiles_n + tn;
@@ -477,9 +752,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       acc.ws = ws_tile;
     }
     if (run) {
-      const float ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, 0, 1);
+      const float ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, 0, 1, pre);
       if constexpr (EPI == EPI_RESID) store_row_sumsq(g, tm, tn, row, ss);
     }
+    if (threadIdx.x == 64) trace_at(g, TR_END);
   }
 
   tc_fence_before();
@@ -553,8 +829,11 @@ int gemm_max_active_clusters(int bn, int cluster, int* out) {
   }
 }
 
+unsigned long long* g_debug_trace = nullptr;
+
 int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb, GemmArgs g,
                 cudaStream_t stream) {
+  g.trace = g_debug_trace;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return arg_err("M, N, K must be positive");
   if ((lda * 2) % 16 || (ldb * 2) % 16 || lda < g.K || ldb < g.K)
     return arg_err("lda/ldb: rows must be 16-byte multiples and >= K");

@@ -30,6 +30,31 @@ enum EpiKind : int {
   EPI_RESID = 4,   // h += acc; hg = bf16(h * g_next); per-tile sum(h^2)
 };
 
+constexpr int TB_MAX_RANKS = 8;
+
+// Device view of a tensor-parallel communicator (comm.cu).  Every rank owns
+// one allocation with the same layout; rs/ag/flags[p] point into rank p's
+// allocation (peer-mapped for p != rank).
+//   rs[p]    [2 parity][world src][plane] bf16: partial sums pushed by each
+//            source rank (one-shot: every column; two-shot: the columns rank
+//            p owns); a plane holds a whole output tile by tile, each tile as
+//            [16-column unit][half][128 rows][8 columns]
+//   ag[p]    [2 parity][plane] bf16: reduced sums (two-shot)
+//   flags[p] [2 kind][2 parity][world src][max_ctas] u32: "source src's CTA
+//            c has delivered call `epoch`" (kind 0: partials, 1: sums)
+//   state    this rank's step counter; a call's epoch is
+//            state[0] * n_sites + site + 1, its parity epoch & 1
+struct CommDev {
+  int rank, world;  // world <= 1: no all-reduce
+  int two_shot;
+  int site, n_sites;
+  int max_rows, n_cols, max_ctas;
+  uint32_t* state;
+  __nv_bfloat16* rs[TB_MAX_RANKS];
+  __nv_bfloat16* ag[TB_MAX_RANKS];
+  uint32_t* flags[TB_MAX_RANKS];
+};
+
 struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n, splits, group_m;
@@ -66,6 +91,26 @@ struct GemmArgs {
   int sq2_ld;
   // EPI_SWIGLU
   int n_feat;
+  // EPI_RESID across tensor-parallel ranks (comm.world > 1)
+  CommDev comm;
+  // debug timeline (tb_debug_trace): per CTA 16 globaltimer stamps, or null
+  unsigned long long* trace;
+};
+
+// Timeline points recorded when GemmArgs::trace is set.
+enum TracePoint : int {
+  TR_START = 0,       // CTA set up (barriers, TMEM)
+  TR_LOADS_ISSUED,    // producer issued its last TMA load
+  TR_ACC_READY,       // epilogue saw the accumulator complete
+  TR_PUSHED,          // partials pushed and fenced (all-reduce)
+  TR_PARTNERS,        // partner flags observed (all-reduce)
+  TR_SUMS,            // reduced sums delivered (two-shot)
+  TR_END,             // epilogue done
+  TR_PARKED,          // cluster split: partial parked in shared memory
+  TR_CLUSTER_SYNC,    // cluster split: every member parked
+  TR_BODY,            // cluster split: reduction + epilogue body done
+  TR_COMBINED,        // cluster split: row sums combined
+  TR_POINTS = 16,
 };
 
 }  // namespace tb

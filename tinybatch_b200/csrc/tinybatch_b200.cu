@@ -5,4 +5,5 @@
 #include "attention.cu"
 #include "misc.cu"
 #include "capi.cu"
+#include "comm.cu"
 #include "static_scratch.cu"

@@ -340,16 +340,20 @@ class DeviceModel:
             self._alloc(max(T, self.T_max), max(S, self.S_max))
 
     # one row-parallel projection: residual (+ all-reduce) + norm prologue
-    def _row(self, x, wmat, g_next, T, last: bool, md: StepMeta):
+    def _row(self, x, wmat, g_next, T, last: bool, md: StepMeta, site: int):
         bn, splits = plan_gemm(T, wmat.shape[0], wmat.shape[1])
         kw = dict(bn=bn, splits=splits, scratch=self.scratch)
         if last:
             kw.update(row_dst=md.row_dst, hg2=self.hg_last, sq2=self.sq_last)
         Nn, K = wmat.shape
         nbytes = 2 * Nn * K + 2 * T * K + T * Nn * (4 + 4 + 2)
-        fn = ops.row_linear_residual if self.comm is None else self.comm.row_linear_residual
-        self._run("row_gemm_residual", nbytes, 2.0 * T * Nn * K, fn, x, wmat, self.h[:T], g_next,
-                  self.hg[:T], self.sq, **kw)
+        if self.comm is None:
+            self._run("row_gemm_residual", nbytes, 2.0 * T * Nn * K, ops.row_linear_residual, x,
+                      wmat, self.h[:T], g_next, self.hg[:T], self.sq, **kw)
+        else:
+            self._run("row_gemm_allreduce_residual", nbytes, 2.0 * T * Nn * K,
+                      self.comm.row_linear_residual, x, wmat, self.h[:T], g_next, self.hg[:T],
+                      self.sq, site=site, n_sites=2 * self.cfg.n_layers, **kw)
         return -(-Nn // bn)
 
     def forward(self, md: StepMeta, kv_pools: list[torch.Tensor], compute_logits: bool = True,
@@ -363,6 +367,8 @@ class DeviceModel:
         d, hd = cfg.d_model, cfg.head_dim
         inv_d, eps = 1.0 / d, cfg.rms_eps
         bs = kv_pools[0].shape[3]
+        if self.comm is not None:
+            self.comm.begin_step()
         self._run("embed", T * d * (2 + 4 + 2), 0.0, ops.embed, md.ids, W.emb, W.layers[0].ln_in,
                   self.h[:T], self.hg[:T], self.sq[0])
         kv_row = 2 * W.n_kv * hd * 2          # K+V bytes of one token in one layer
@@ -396,7 +402,7 @@ class DeviceModel:
                     4.0 * md.pre_pairs * W.n_q * hd, ops.paged_attention_prefill,
                     self.q, self.attn, pool, block_tables=md.pre_bt, q_start=md.pre_q_start,
                     q_len=md.pre_q_len, ctx_len=md.pre_ctx, work=md.work, **akw)
-            parts = self._row(self.attn[:T], L.wo, L.ln_post, T, False, md)
+            parts = self._row(self.attn[:T], L.wo, L.ln_post, T, False, md, 2 * li)
             bn = RankWeights.GU_BN
             _, splits = plan_gemm(T, L.wgu.shape[0], d, bns=(bn,))
             Ngu = L.wgu.shape[0]
@@ -406,7 +412,7 @@ class DeviceModel:
                       scratch=self.scratch)
             last = li == len(W.layers) - 1
             g_next = W.final_norm if last else W.layers[li + 1].ln_in
-            parts = self._row(self.act[:T, :W.ff], L.wd, g_next, T, last, md)
+            parts = self._row(self.act[:T, :W.ff], L.wd, g_next, T, last, md, 2 * li + 1)
         if not compute_logits:
             return None
         bn, splits = plan_gemm(n, cfg.vocab_size, d)

@@ -20,6 +20,7 @@
 from __future__ import annotations
 
 import os
+import pickle
 import time
 
 import torch
@@ -62,7 +63,8 @@ def _rank_model(w: dict, cfg: ModelConfig, world: int):
         comm = None
         if world > 1:
             from .comm import TPComm
-            comm = TPComm.from_process_group(torch.device("cuda", torch.cuda.current_device()))
+            comm = TPComm.from_process_group(torch.device("cuda", torch.cuda.current_device()),
+                                             n_cols=cfg.d_model, max_rows=4096)
         dev = torch.device("cuda", torch.cuda.current_device())
         model = Qwen2Paged.from_weights(cfg, w, device=dev, rank=rank, world=world, comm=comm,
                                         sharded=True)
@@ -92,8 +94,8 @@ def tp_forward(token_ids: torch.Tensor, w: dict, cfg: ModelConfig, world: int,
     return out.cpu() if token_ids.device.type == "cpu" else out
 
 
-def _worker(rank: int, world: int, w: dict, cfg: ModelConfig, token_ids: torch.Tensor,
-            port: int, queue, timeout_s: float) -> None:
+def _worker(rank: int, world: int, port: int, w: dict, cfg: ModelConfig,
+            token_ids: torch.Tensor, timeout_s: float, queue) -> None:
     import datetime
     torch.cuda.set_device(rank)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -109,15 +111,78 @@ def _worker(rank: int, world: int, w: dict, cfg: ModelConfig, token_ids: torch.T
         torch.cuda.synchronize()
         stats["wall_seconds"] = time.perf_counter() - t0
         if rank == 0:
-            queue.put((logits.cpu(), stats))
-    except BaseException as e:  # report instead of leaving rank 0's caller waiting
-        if rank == 0:
-            queue.put(e)
-        raise
+            queue.put((0, (logits.cpu(), stats)))
     finally:
         from .comm import close_all
         close_all()
         dist.destroy_process_group()
+
+
+class _Reporter:
+    """Queue front that sends every report by value (plain pickle), so a
+    tensor in it stays readable after the sending rank has exited."""
+
+    def __init__(self, queue):
+        self._q = queue
+
+    def put(self, item) -> None:
+        self._q.put(pickle.dumps(item))
+
+
+def _entry(target, rank, world, port, args, queue):
+    """Process body: run ``target``; report an exception to the parent."""
+    rep = _Reporter(queue)
+    try:
+        target(rank, world, port, *args, rep)
+    except BaseException as e:  # the parent turns this into a RuntimeError
+        rep.put((rank, RuntimeError(f"rank {rank}: {e!r}")))
+        raise
+
+
+def _spawn(world: int, target, args: tuple, port: int, timeout_s: float,
+           collect_all: bool = False) -> list:
+    """Run ``target(rank, world, port, *args, queue)`` in ``world`` spawned
+    processes; each rank reports ``queue.put((rank, payload))`` (rank 0 only
+    unless ``collect_all``).  Returns the payloads indexed by rank.  Raises
+    ``RuntimeError`` when a rank reports an exception, exits with an error,
+    or the results do not arrive within ``timeout_s``; surviving processes
+    are then killed, so a dead rank never leaves the caller waiting."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.SimpleQueue()
+    procs = [ctx.Process(target=_entry, args=(target, r, world, port, args, queue))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    need = world if collect_all else 1
+    got: dict[int, object] = {}
+    error = None
+    deadline = time.time() + timeout_s
+    while len(got) < need and error is None:
+        while not queue.empty():
+            rank, payload = pickle.loads(queue.get())
+            if isinstance(payload, BaseException):
+                error = payload
+                break
+            got[rank] = payload
+        if error is None and len(got) < need:
+            dead = [(i, p.exitcode) for i, p in enumerate(procs) if p.exitcode not in (None, 0)]
+            if dead:
+                error = RuntimeError(f"rank(s) exited with errors: {dead}")
+            elif time.time() > deadline:
+                error = RuntimeError(f"no result within {timeout_s:.0f} s")
+            else:
+                time.sleep(0.02)
+    for p in procs:
+        p.join(timeout=5.0 if error is None else 0.5)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    if error is not None:
+        raise RuntimeError(f"tensor-parallel run failed: {error}")
+    if not collect_all:
+        return [got[0]]
+    return [got[r] for r in range(world)]
 
 
 def run_tp_forward(world: int, w: dict, cfg: ModelConfig, token_ids: torch.Tensor,
@@ -127,32 +192,4 @@ def run_tp_forward(world: int, w: dict, cfg: ModelConfig, token_ids: torch.Tenso
     exceeds ``timeout_s``."""
     if torch.cuda.device_count() < world:
         raise RuntimeError(f"run_tp_forward needs {world} GPUs, found {torch.cuda.device_count()}")
-    ctx = mp.get_context("spawn")
-    queue = ctx.SimpleQueue()
-    procs = [ctx.Process(target=_worker, args=(r, world, w, cfg, token_ids, port, queue, timeout_s))
-             for r in range(world)]
-    for p in procs:
-        p.start()
-    deadline = time.time() + timeout_s
-    result = None
-    while result is None:
-        if not queue.empty():
-            result = queue.get()
-            break
-        dead = [p for p in procs if p.exitcode not in (None, 0)]
-        if dead:
-            break
-        if time.time() > deadline:
-            break
-        time.sleep(0.05)
-    for p in procs:
-        p.join(timeout=max(1.0, deadline - time.time()))
-        if p.is_alive():
-            p.kill()
-            p.join()
-    if result is None:
-        codes = [p.exitcode for p in procs]
-        raise RuntimeError(f"tensor-parallel forward failed or timed out (exit codes {codes})")
-    if isinstance(result, BaseException):
-        raise RuntimeError(f"rank 0 failed: {result!r}")
-    return result
+    return _spawn(world, _worker, (w, cfg, token_ids, timeout_s), port, timeout_s)[0]
