@@ -48,10 +48,10 @@ const char* tb_last_error(void);
 
 /* Debug timeline: while buf is not NULL, every GEMM launched afterwards by
  * this process writes, per CTA c, %globaltimer stamps (ns) to buf[16*c + k]
- * for k = 0 start, 1 loads issued, 2 accumulator ready, 3 partials pushed,
- * 4 partners seen, 5 sums delivered, 6 end, 7 partial parked, 8 cluster
- * synced, 9 epilogue body done, 10 row sums combined (unreached points are
- * left as they were).  buf must hold 16 entries per CTA of the largest
+ * for k = 0 start, 1 loads issued, 2 accumulator ready, 3 partials pushed
+ * to the peer ranks, 4 partners seen, 5 sums delivered, 6 end, 7 split-K
+ * chunks stored to their cluster owners, 8 every cluster member's chunks
+ * arrived (unreached points are left as they were).  buf must hold 16 entries per CTA of the largest
  * launch.  Not thread-safe; NULL turns it off. */
 int tb_debug_trace(unsigned long long* buf);
 
@@ -70,9 +70,13 @@ int tb_status(unsigned int* code_h, int clear);
  *   bn: output tile width (64, 128, 192 or 256); splits: split-K factor.
  *   ws/ws_bytes: how split-K partials are combined.
  *     ws == NULL, splits in 2..8: the splits of an output tile run as one
- *       thread-block cluster; each CTA parks its fp32 partial in its shared
- *       memory and reduces a slice of the tile's columns over distributed
- *       shared memory, in split order (deterministic, no scratch).
+ *       thread-block cluster; each CTA stores every 16-column chunk of its
+ *       fp32 partial into the shared memory of the member that owns the
+ *       chunk (distributed shared memory), and each owner sums its chunks in
+ *       split order (deterministic, no scratch) and finishes them.  The
+ *       chunks a member receives must fit its pipeline buffers: calls whose
+ *       (bn, splits) do not fit fail with TB_ERR_ARG (bn 256 with 7 splits
+ *       for the gate/up and the head_dim >= 32 QKV projections).
  *     ws != NULL: partials go through caller scratch of at least
  *       tb_gemm_scratch_bytes(M, N, bn, splits) bytes: a fixed 64 KiB region
  *       of per-tile arrival counters (zero when first handed over, left zero
@@ -81,6 +85,20 @@ int tb_status(unsigned int* code_h, int clear);
  *     Unused when splits == 1.
  */
 size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits);
+
+/* Optional L2 warm-up carried by a GEMM call for the weight the NEXT kernel
+ * streams (decode steps are weight-bound; a GEMM's epilogue leaves HBM idle).
+ * Once a CTA's main loop is done, the library issues L2 prefetches of the
+ * first `bytes` of every (row, K segment) of the bf16 matrix [rows, k] with
+ * row pitch ld elements, the K segments being the next call's split-K ranges
+ * (splits of ceil(k/64) 64-column blocks).  A hint: results never depend on
+ * it.  base 16-byte aligned, ld a multiple of 8, bytes a multiple of 16.
+ * Pass NULL (or base == NULL) for none. */
+typedef struct tb_l2_prefetch {
+  const void* base;
+  long long ld;
+  int rows, k, splits, bytes;
+} tb_l2_prefetch;
 
 /* How many clusters of `cluster` GEMM CTAs (tile width bn) fit on the current
  * device at once (cudaOccupancyMaxActiveClusters); for choosing splits. */
@@ -92,7 +110,7 @@ int tb_gemm_max_active_clusters(int bn, int cluster, int* out_h);
 int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
               const float* sq, int sq_parts, int sq_ld, float inv_d, float eps,
               void* out, int ld_out, int out_f32, int bn, int splits,
-              void* ws, size_t ws_bytes, void* stream);
+              void* ws, size_t ws_bytes, const tb_l2_prefetch* next, void* stream);
 
 /* Bytes of split-K scratch built into the library for
  * tb_linear_static_scratch: 4 KiB of arrival counters (at most 1024 output
@@ -107,7 +125,7 @@ int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int 
  * that scratch from a fixed array inside the library
  * (TB_STATIC_SCRATCH_BYTES per device, held by every GPU that loads the
  * library until the process exits) and allocates nothing.  Arguments and
- * result are those of tb_linear without ws/ws_bytes.
+ * result are those of tb_linear without ws/ws_bytes and next.
  *   - A call whose split-K scratch would exceed the array (or 1024 tiles)
  *     fails with TB_ERR_ARG and a message naming the size it needed.
  *   - The first call on a device looks up the array's device address
@@ -136,7 +154,8 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
                    const float* rope_cos, const float* rope_sin, int max_pos,
                    const int* positions, const int* slots,
                    void* q_out, int ld_q, void* kv_pool, int block_size,
-                   int bn, int splits, void* ws, size_t ws_bytes, void* stream);
+                   int bn, int splits, void* ws, size_t ws_bytes,
+                   const tb_l2_prefetch* next, void* stream);
 
 /* Column-parallel gate/up projection with SwiGLU epilogue.  w_gu holds, for
  * each output tile t of width bn, the bn/2 gate rows of features
@@ -147,22 +166,23 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
 int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, int K,
                       int n_feat, const float* sq, int sq_parts, int sq_ld, float inv_d,
                       float eps, void* act, int ld_act, int bn, int splits,
-                      void* ws, size_t ws_bytes, void* stream);
+                      void* ws, size_t ws_bytes, const tb_l2_prefetch* next, void* stream);
 
 /* Row-parallel projection + residual + next-norm prologue, single rank:
  *   h[m, :] += x . w^T  (fp32 residual stream, in place)
- *   hg = bf16(h * g_next), sq_out[tile_n, m] = sum over the tile's columns of h^2
+ *   hg = bf16(h * g_next), sq_out[part, m] = partial sums of h^2 over the row
  * so the next GEMM applies rms_norm(h) * g_next through its rowscale.
  * Optional gather: when row_dst is not NULL and row_dst[m] >= 0, row m of hg
  * and of sq_out is also written to row row_dst[m] of hg2 / sq2.
  * Replaces h + F.linear(attn, Wo) / h + F.linear(act, Wd) and the following
  * _rms_norm (src/tinybatch/model.py:149-151,154,156; tensor_parallel.py:108-110,114,116).
- * The number of sq parts written is ceil(N / bn). */
+ * The number of sq parts written is ceil(N / bn), times splits with cluster
+ * split-K (ws == NULL, splits > 1: one part per cluster member). */
 int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
                            float* h, int ld_h, const void* g_next, void* hg, int ld_hg,
                            float* sq_out, int sq_out_ld, const int* row_dst, void* hg2,
                            float* sq2, int sq2_ld, int bn, int splits, void* ws,
-                           size_t ws_bytes, void* stream);
+                           size_t ws_bytes, const tb_l2_prefetch* next, void* stream);
 
 /* ------------------------------------------------- tensor-parallel comm
  * One communicator per rank (one process per GPU).  It owns one device
@@ -197,7 +217,8 @@ int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int 
                                      int K, float* h, int ld_h, const void* g_next, void* hg,
                                      int ld_hg, float* sq_out, int sq_out_ld, const int* row_dst,
                                      void* hg2, float* sq2, int sq2_ld, void* comm, int site,
-                                     int n_sites, int two_shot, int bn, int splits, void* stream);
+                                     int n_sites, int two_shot, int bn, int splits,
+                                     const tb_l2_prefetch* next, void* stream);
 
 /* ------------------------------------------------------------- attention
  * Paged GQA attention reading K/V through block tables (no gather copy).
@@ -210,7 +231,14 @@ int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int 
  *
  * _decode: every sequence must have q_len*Hq/Hkv <= 16 (decode steps).
  *   Keys are split into pieces of split_tokens (a multiple of 16); grid is
- *   sized for max_ctx.  Scratch: tb_attention_scratch_bytes.
+ *   sized for max_ctx.  Scratch: tb_attention_scratch_bytes, zero-filled
+ *   before its first use; its first 64 KiB hold per-(seq, kv head) arrival
+ *   counters that every completed call leaves at zero (the last split CTA
+ *   of a pair merges the splits in split order, in the same launch).
+ *   At most 16384 (sequence, kv head) pairs per call with more than one split.
+ *   split_tokens <= 8192.  seq_order (optional, [n_seqs] int32, a
+ *   permutation): sequences are dispatched in this order (longest first
+ *   keeps the tail of the launch short); NULL = index order.
  * _prefill: any q_len; work_pairs [n_work, 2] int32 = (seq, 64-row tile). */
 size_t tb_attention_scratch_bytes(int n_seqs, int n_kv_heads, int head_dim, int max_ctx,
                                   int split_tokens);
@@ -218,8 +246,9 @@ int tb_paged_attention_decode(const void* q, int ld_q, void* out, int ld_out,
                               const void* kv_pool, int num_blocks, int n_q_heads,
                               int n_kv_heads, int head_dim, int block_size,
                               const int* block_tables, int bt_ld, const int* q_start,
-                              const int* q_len, const int* ctx_len, int n_seqs, int max_ctx,
-                              int split_tokens, void* ws, size_t ws_bytes, void* stream);
+                              const int* q_len, const int* ctx_len, const int* seq_order,
+                              int n_seqs, int max_ctx, int split_tokens, void* ws,
+                              size_t ws_bytes, void* stream);
 int tb_paged_attention_prefill(const void* q, int ld_q, void* out, int ld_out,
                                const void* kv_pool, int num_blocks, int n_q_heads,
                                int n_kv_heads, int head_dim, int block_size,

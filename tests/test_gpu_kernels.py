@@ -50,6 +50,7 @@ GEMM_CASES = [
     (130, 256, 4096, 256, 5),
     (128, 960, 2048, 192, 4),
     (100, 384, 4096, 64, 8),
+    (128, 1280, 2048, 256, 6),
 ]
 
 
@@ -84,7 +85,8 @@ def test_linear_rowscale_bf16():
 @pytest.mark.parametrize("M,N,K,bn,splits,mode", [
     (128, 512, 640, 128, 1, "cluster"), (37, 256, 1024, 64, 4, "global"),
     (37, 256, 1024, 64, 4, "cluster"), (260, 896, 896, 128, 1, "cluster"),
-    (128, 5120, 5120, 256, 7, "cluster"), (96, 896, 896, 192, 3, "cluster")])
+    (128, 5120, 5120, 256, 7, "cluster"), (96, 896, 896, 192, 3, "cluster"),
+    (128, 2048, 2048, 256, 8, "cluster"), (20, 640, 1280, 128, 5, "cluster")])
 def test_row_linear_residual(M, N, K, bn, splits, mode):
     x = _rand(M, K, seed=5)
     w = _rand(N, K, scale=1 / math.sqrt(K), seed=6)
@@ -92,7 +94,7 @@ def test_row_linear_residual(M, N, K, bn, splits, mode):
     g = _rand(N, seed=7) + 1.0
     h = h0.clone()
     hg = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
-    parts = (N + bn - 1) // bn
+    parts = ops.row_parts(N, bn, splits, mode)
     sq = torch.empty(parts, M, device=DEV)
     row_dst = torch.full((M,), -1, dtype=torch.int32, device=DEV)
     row_dst[M - 1] = 0
@@ -114,7 +116,8 @@ def test_row_linear_residual(M, N, K, bn, splits, mode):
 @pytest.mark.parametrize("M,F,K,bn,splits,mode", [
     (128, 256, 512, 128, 1, "cluster"), (50, 192, 896, 128, 2, "global"),
     (50, 192, 896, 128, 2, "cluster"), (200, 128, 256, 256, 1, "cluster"),
-    (128, 1728, 640, 192, 2, "cluster"), (128, 864, 1024, 192, 1, "cluster")])
+    (128, 1728, 640, 192, 2, "cluster"), (128, 864, 1024, 192, 1, "cluster"),
+    (128, 992, 1024, 256, 3, "cluster"), (64, 720, 1280, 192, 5, "cluster")])
 def test_gate_up_swiglu(M, F, K, bn, splits, mode):
     x = _rand(M, K, seed=8)
     wg = _rand(F, K, scale=1 / math.sqrt(K), seed=9)
@@ -141,9 +144,10 @@ def test_gate_up_swiglu(M, F, K, bn, splits, mode):
 @pytest.mark.parametrize("hq,hkv,hd,bn,bs,splits", [
     (4, 2, 16, 64, 16, 1), (14, 2, 64, 128, 16, 1), (40, 8, 128, 128, 16, 1),
     (5, 1, 128, 256, 4, 1), (40, 8, 128, 256, 16, 4), (14, 2, 64, 192, 16, 2),
-    (5, 1, 128, 128, 16, 3)])
+    (5, 1, 128, 128, 16, 3), (4, 2, 16, 64, 16, 2), (14, 2, 64, 256, 16, 3),
+    (40, 8, 128, 256, 16, 5)])
 def test_qkv_rope_kv(hq, hkv, hd, bn, bs, splits):
-    M, K = 70, 256
+    M, K = 70, max(256, 128 * splits)
     N = (hq + 2 * hkv) * hd
     x = _rand(M, K, seed=11)
     w = _rand(N, K, scale=1 / math.sqrt(K), seed=12)
@@ -175,6 +179,22 @@ def test_qkv_rope_kv(hq, hkv, hd, bn, bs, splits):
         b, o = int(slots[m]) // bs, int(slots[m]) % bs
         torch.testing.assert_close(pc[b, 0, :, o], kr[m], atol=1.6e-2, rtol=1.6e-2)
         torch.testing.assert_close(pc[b, 1, :, o], vr[m], atol=1.6e-2, rtol=1.6e-2)
+
+
+def test_cluster_split_that_does_not_fit_is_rejected():
+    """bn 256 with 7 cluster members: the RoPE-paired chunks one member
+    receives exceed its pipeline buffers; the launcher refuses the call."""
+    hq, hkv, hd, M, K = 40, 8, 128, 16, 1024
+    N = (hq + 2 * hkv) * hd
+    cos, sin = R.rope_tables(torch.arange(64), hd, 1e6)
+    with pytest.raises(_native.NativeError, match="do not fit"):
+        ops.qkv_rope_kv(_rand(M, K), _rand(N, K), _rand(N), n_q_heads=hq, n_kv_heads=hkv,
+                        head_dim=hd, sq=None, inv_d=0.0, eps=0.0, rope_cos=cos.to(DEV),
+                        rope_sin=sin.to(DEV), positions=torch.zeros(M, dtype=torch.int32, device=DEV),
+                        slots=torch.zeros(M, dtype=torch.int32, device=DEV),
+                        q_out=torch.empty(M, hq * hd, dtype=torch.bfloat16, device=DEV),
+                        kv_pool=torch.zeros(4, 2, hkv, 16, hd, dtype=torch.bfloat16, device=DEV),
+                        block_size=16, bn=256, splits=7)
 
 
 def _paged_case(hq, hkv, hd, bs, q_lens, ctx_lens, seed=0):
@@ -212,17 +232,29 @@ def _paged_case(hq, hkv, hd, bs, q_lens, ctx_lens, seed=0):
 
 @pytest.mark.parametrize("hq,hkv,hd,bs", [(40, 8, 128, 16), (14, 2, 64, 16), (4, 2, 16, 4),
                                           (64, 8, 128, 16)])
-@pytest.mark.parametrize("split_tokens", [512, 64])
-def test_paged_attention_decode(hq, hkv, hd, bs, split_tokens):
-    ctx = [1, 15, 16, 17, 100, 700, 1300, 33]
+@pytest.mark.parametrize("split_tokens,ordered", [(512, False), (64, False), (4096, True),
+                                                  (256, True)])
+def test_paged_attention_decode(hq, hkv, hd, bs, split_tokens, ordered):
+    """Split-KV (merged in the launch by the last split of each sequence and
+    kv head) and one-CTA-per-sequence decode, in index order or dispatched
+    longest first."""
+    ctx = [1, 15, 16, 17, 100, 700, 1300, 33, 3000]
     d, ref = _paged_case(hq, hkv, hd, bs, [1] * len(ctx), ctx, seed=3)
     out = torch.zeros(len(ctx), hq * hd, dtype=torch.bfloat16, device=DEV)
-    ops.paged_attention_decode(d["q"], out, d["pool"], n_q_heads=hq, n_kv_heads=hkv,
-                               head_dim=hd, block_size=bs, block_tables=d["bt"],
-                               q_start=d["q_start"], q_len=d["q_len"], ctx_len=d["ctx"],
-                               max_ctx=max(ctx), split_tokens=split_tokens)
-    torch.cuda.synchronize()
-    torch.testing.assert_close(out.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+    order = None
+    if ordered:
+        order = torch.tensor(sorted(range(len(ctx)), key=lambda i: -ctx[i]), dtype=torch.int32,
+                             device=DEV)
+    arena = ops.Scratch(DEV, 1 << 16)
+    for _ in range(2):   # the second call reuses the arena: arrival counters were reset
+        out.zero_()
+        ops.paged_attention_decode(d["q"], out, d["pool"], n_q_heads=hq, n_kv_heads=hkv,
+                                   head_dim=hd, block_size=bs, block_tables=d["bt"],
+                                   q_start=d["q_start"], q_len=d["q_len"], ctx_len=d["ctx"],
+                                   max_ctx=max(ctx), split_tokens=split_tokens, seq_order=order,
+                                   scratch=arena)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float().cpu(), ref, atol=2e-2, rtol=2e-2)
 
 
 @pytest.mark.parametrize("hq,hkv,hd,bs", [(40, 8, 128, 16), (14, 2, 64, 16), (4, 2, 16, 4)])

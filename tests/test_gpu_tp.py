@@ -50,7 +50,7 @@ def _op_worker(rank, world, port, cases, queue):
     import torch.distributed as dist
 
     from oracle import qwen2_ref as R
-    from tinybatch_b200 import _native
+    from tinybatch_b200 import _native, ops
     from tinybatch_b200.comm import TPComm
 
     torch.cuda.set_device(rank)
@@ -75,7 +75,7 @@ def _op_worker(rank, world, port, cases, queue):
             gn = torch.ones(N, dtype=torch.bfloat16)
             h = h0.to(dev).clone()
             hg = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-            parts = -(-N // bn)
+            parts = ops.row_parts(N, bn, splits)
             sq = torch.empty(parts, M, device=dev)
             comm.begin_step()
             comm.row_linear_residual(xs[rank].to(dev), ws[rank].to(dev), h, gn.to(dev), hg, sq,

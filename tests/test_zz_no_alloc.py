@@ -53,7 +53,7 @@ def _reference(lib, x, w, out, bn, splits):
     ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
     rc = lib.tb_linear(x.data_ptr(), K, w.data_ptr(), K, M, N, K, None, 0, 0, 0.0, 0.0,
                        out.data_ptr(), out.stride(0), 1, bn, splits, ws.data_ptr(), ws.numel(),
-                       torch.cuda.current_stream().cuda_stream)
+                       None, torch.cuda.current_stream().cuda_stream)
     return rc
 
 

@@ -71,7 +71,7 @@ class TPComm:
 
     def row_linear_residual(self, x, w, h, g_next, hg, sq_out, *, site: int, n_sites: int,
                             row_dst=None, hg2=None, sq2=None, bn=128, splits=1,
-                            two_shot: bool | None = None, **_):
+                            two_shot: bool | None = None, next_weight=None, **_):
         """Row-parallel projection + fused all-reduce + residual + norm prologue."""
         M, K = x.shape
         Nn = w.shape[0]
@@ -83,7 +83,8 @@ class TPComm:
             ptr(x), x.stride(0), ptr(w), w.stride(0), M, Nn, K, ptr(h), h.stride(0), ptr(g_next),
             ptr(hg), hg.stride(0), ptr(sq_out), sq_out.stride(0), ptr(row_dst), ptr(hg2), ptr(sq2),
             sq2.stride(0) if sq2 is not None else 0, self._ptr, site, n_sites, int(bool(two_shot)),
-            bn, splits, N.stream_ptr()), "tb_row_linear_allreduce_residual")
+            bn, splits, N.pf_arg(next_weight), N.stream_ptr()),
+            "tb_row_linear_allreduce_residual")
 
     def close(self, barrier: bool = True) -> None:
         if self.closed:

@@ -17,8 +17,10 @@
 //   decode kernels  q_len*G <= 16 rows; one CTA per (split, kv head, seq);
 //                   4 warps take interleaved key chunks of the split and
 //                   merge their (max, sum, O) in shared memory; with more
-//                   than one split the CTA writes (O/l, log2 l + max) and
-//                   attn_combine_kernel merges the splits.  Chunks arrive by
+//                   than one split the CTA writes (O/l, log2 l + max) to the
+//                   workspace and the last split CTA of the (seq, kv head)
+//                   to finish merges all splits in split order (an arrival
+//                   counter per pair, reset by the merging CTA).  Chunks arrive by
 //                   TMA (a producer warp, 8-slot mbarrier ring) when the
 //                   block size is a multiple of 16 and hd is 64 or 128,
 //                   else by per-lane cp.async.
@@ -227,10 +229,36 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, int q0, int G, int kvh
   }
 }
 
+// Merge the n_splits partial results of (seq, kv head) in split order:
+// out = sum_s 2^(lse_s - M) O_s / sum_s 2^(lse_s - M), M = max_s lse_s.
+// The partials were written by other CTAs of this launch: read through L2.
+template <int HD>
+__device__ __forceinline__ void merge_splits(const AttnArgs& a, int seq, int kvh, int n_splits,
+                                             int q0, int G, int nrows) {
+  const size_t base0 = ((size_t)seq * a.n_kv_heads + kvh) * a.max_splits;
+  for (int i = threadIdx.x; i < nrows * HD; i += blockDim.x) {
+    const int r = i / HD, c = i % HD;
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, __ldcg(a.ws_lse + (base0 + s) * 16 + r));
+    const float mu = M == -INFINITY ? 0.f : M;
+    float W = 0.f, acc = 0.f;
+#pragma unroll 4
+    for (int s = 0; s < n_splits; ++s) {
+      const float w = exp2f(__ldcg(a.ws_lse + (base0 + s) * 16 + r) - mu);
+      W += w;
+      acc += w * __ldcg(a.ws_o + ((base0 + s) * 16 + r) * HD + c);
+    }
+    a.out[(size_t)(q0 + r / G) * a.ld_out + (size_t)(kvh * G + r % G) * HD + c] =
+        __float2bfloat16_rn(W > 0.f ? acc / W : 0.f);
+  }
+}
+
 // Merge the per-warp flash states of nw warps (smem: O[nw][16][HD] fp32,
-// m[nw][16], l[nw][16]) and write the normalised rows: straight to `out`
-// when the sequence has one split, else (O/l, max + log2 l) to the split
-// workspace.  Called by every thread of the CTA after the key loop.
+// m[nw][16], l[nw][16], then one int) and write the normalised rows:
+// straight to `out` when the sequence has one split, else (O/l, max +
+// log2 l) to the split workspace, after which the last split CTA of this
+// (seq, kv head) to arrive merges every split.  Called by every thread of the
+// CTA after the key loop.
 template <int HD, class F>
 __device__ __forceinline__ void merge_warps(const AttnArgs& a, F& f, uint8_t* smem, int nw,
                                             int warp, int lane, int seq, int kvh, int split,
@@ -279,6 +307,22 @@ __device__ __forceinline__ void merge_warps(const AttnArgs& a, F& f, uint8_t* sm
       if (c == 0) a.ws_lse[base] = L > 0.f ? mu + log2f(L) : -INFINITY;
     }
   }
+  if (direct) return;
+  // publish this split, then count arrivals; the last CTA merges
+  int* last = reinterpret_cast<int*>(sl + nw * 16);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* cnt = a.ws_count + (size_t)seq * a.n_kv_heads + kvh;
+    const int prev = atomicAdd(cnt, 1);
+    const int is_last = prev == n_splits - 1;
+    if (is_last) *cnt = 0;   // ready for the next call
+    *last = is_last;
+  }
+  __syncthreads();
+  if (!*last) return;
+  __threadfence();
+  merge_splits<HD>(a, seq, kvh, n_splits, q0, G, nrows);
 }
 
 constexpr int DEC_STAGES = 3;
@@ -289,8 +333,13 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_wait();
   if (threadIdx.x == 0) pdl_trigger();
-  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int seq = a.seq_order != nullptr ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (seq < 0 || seq >= a.n_seqs) {
+    if (threadIdx.x == 0) set_status(ERR_BAD_INDEX);
+    return;
+  }
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
   const int nrows = qlen * G;
@@ -356,7 +405,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
 // by mbarriers; warps 0-3 consume chunks round-robin and merge at the end.
 constexpr int TMA_STAGES = 8;
 constexpr int TMA_THREADS = 160;
-constexpr int TMA_MAX_SPLIT_CHUNKS = 128;   // split_tokens <= 2048
+constexpr int TMA_MAX_SPLIT_CHUNKS = 512;   // split_tokens <= 8192
 // Chunk i goes to slot i % TMA_STAGES and to consumer warp i % 4.  With the
 // stage count a multiple of 4 every slot has a single consumer warp, which
 // waits on its slot's phases strictly in order; otherwise a warp could wait
@@ -370,16 +419,22 @@ __global__ void __launch_bounds__(TMA_THREADS, 3)
   using C = TmaChunkLayout<HD>;
   constexpr int SLOT = 2 * C::BYTES;  // K then V
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + TMA_STAGES * SLOT);
   uint64_t* empty = full + TMA_STAGES;
   int* chunk_row = reinterpret_cast<int*>(empty + TMA_STAGES);  // [split_chunks] pool row of K
 
-  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, kvh = blockIdx.y;
   // step metadata and block tables come from host copies, not from the
   // previous kernel: read them before waiting
+  const int seq = a.seq_order != nullptr ? a.seq_order[blockIdx.z] : (int)blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (seq < 0 || seq >= a.n_seqs) {
+    if (threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) set_status(ERR_BAD_INDEX);
+    return;
+  }
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
   const int nrows = qlen * G;
@@ -467,36 +522,6 @@ __global__ void __launch_bounds__(TMA_THREADS, 3)
   merge_warps<HD>(a, f, smem, 4, warp, lane, seq, kvh, split, n_splits, q0, G, nrows, warp < 4);
 }
 
-// Merge decode splits: one CTA per (kv head, seq); skips sequences that fit
-// one split (their output was written directly).
-template <int HD>
-__global__ void attn_combine_kernel(const AttnArgs a) {
-  pdl_wait();
-  if (threadIdx.x == 0) pdl_trigger();
-  const int kvh = blockIdx.x, seq = blockIdx.y;
-  const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
-  const int G = a.n_q_heads / a.n_kv_heads;
-  const int nrows = qlen * G;
-  const int n_chunks = (ctx + 15) / 16;
-  const int n_splits = (n_chunks + a.split_chunks - 1) / a.split_chunks;
-  if (n_splits <= 1 || nrows > 16) return;
-  const size_t base0 = ((size_t)seq * a.n_kv_heads + kvh) * a.max_splits;
-  for (int i = threadIdx.x; i < nrows * HD; i += blockDim.x) {
-    const int r = i / HD, c = i % HD;
-    float M = -INFINITY;
-    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, a.ws_lse[(base0 + s) * 16 + r]);
-    const float mu = M == -INFINITY ? 0.f : M;
-    float W = 0.f, acc = 0.f;
-    for (int s = 0; s < n_splits; ++s) {
-      const float w = exp2f(a.ws_lse[(base0 + s) * 16 + r] - mu);
-      W += w;
-      acc += w * a.ws_o[((base0 + s) * 16 + r) * HD + c];
-    }
-    a.out[(size_t)(q0 + r / G) * a.ld_out + (size_t)(kvh * G + r % G) * HD + c] =
-        __float2bfloat16_rn(W > 0.f ? acc / W : 0.f);
-  }
-}
-
 constexpr int PF_STAGES = 2;
 
 template <int HD>
@@ -571,10 +596,10 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
 template <int HD>
 static int decode_tma_launch(const AttnArgs& a, cudaStream_t st) {
   constexpr int SLOT = 2 * TmaChunkLayout<HD>::BYTES;
-  const int merge = (4 * 16 * (HD + 4) + 2 * 4 * 16) * 4;
+  const int merge = (4 * 16 * (HD + 4) + 2 * 4 * 16) * 4 + 16;
   const int ring = TMA_STAGES * SLOT + 2 * TMA_STAGES * 8 + TMA_MAX_SPLIT_CHUNKS * 4;
   const int smem = (ring > merge ? ring : merge) + 1024;
-  if (a.split_chunks > TMA_MAX_SPLIT_CHUNKS) return arg_err("split_tokens above 2048");
+  if (a.split_chunks > TMA_MAX_SPLIT_CHUNKS) return arg_err("split_tokens above 8192");
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attn_decode_tma_kernel<HD>,
@@ -590,17 +615,14 @@ static int decode_tma_launch(const AttnArgs& a, cudaStream_t st) {
   const uint64_t rows = (uint64_t)a.num_blocks * 2 * a.n_kv_heads * a.block_size;
   int rc = make_tmap_2d(&map, a.pool, HD, rows, (uint64_t)HD * 2, 64, 16);
   if (rc) return rc;
-  rc = launch_pdl(attn_decode_tma_kernel<HD>, dim3(a.max_splits, a.n_kv_heads, a.n_seqs),
-                  dim3(TMA_THREADS), smem, st, 1, "attention decode launch", map, a);
-  if (rc || a.max_splits <= 1) return rc;
-  return launch_pdl(attn_combine_kernel<HD>, dim3(a.n_kv_heads, a.n_seqs), dim3(128), 0, st, 1,
-                    "attention combine launch", a);
+  return launch_pdl(attn_decode_tma_kernel<HD>, dim3(a.max_splits, a.n_kv_heads, a.n_seqs),
+                    dim3(TMA_THREADS), smem, st, 1, "attention decode launch", map, a);
 }
 
 template <int HD>
 static int decode_launch(const AttnArgs& a, cudaStream_t st) {
   const int smem_ring = 4 * DEC_STAGES * 2 * ChunkLayout<HD>::BYTES;
-  const int smem_merge = (4 * 16 * (HD + 4) + 2 * 4 * 16) * 4;
+  const int smem_merge = (4 * 16 * (HD + 4) + 2 * 4 * 16) * 4 + 16;
   const int smem = smem_ring > smem_merge ? smem_ring : smem_merge;
   static bool attr = false;
   if (!attr) {
@@ -609,11 +631,8 @@ static int decode_launch(const AttnArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return host_err(e, "attention smem attribute");
     attr = true;
   }
-  int rc = launch_pdl(attn_decode_kernel<HD>, dim3(a.max_splits, a.n_kv_heads, a.n_seqs),
-                      dim3(128), smem, st, 1, "attention decode launch", a);
-  if (rc || a.max_splits <= 1) return rc;
-  return launch_pdl(attn_combine_kernel<HD>, dim3(a.n_kv_heads, a.n_seqs), dim3(128), 0, st, 1,
-                    "attention combine launch", a);
+  return launch_pdl(attn_decode_kernel<HD>, dim3(a.max_splits, a.n_kv_heads, a.n_seqs),
+                    dim3(128), smem, st, 1, "attention decode launch", a);
 }
 
 template <int HD>
@@ -636,7 +655,8 @@ int attn_decode(AttnArgs a, int head_dim, cudaStream_t st) {
   if (rc) return rc;
   if (a.n_q_heads / a.n_kv_heads > 16) return arg_err("GQA group larger than 16");
   if (a.split_chunks <= 0 || a.max_splits <= 0) return arg_err("split sizes");
-  if (a.max_splits > 1 && (a.ws_o == nullptr || a.ws_lse == nullptr)) return arg_err("split workspace");
+  if (a.max_splits > 1 && (a.ws_o == nullptr || a.ws_lse == nullptr || a.ws_count == nullptr))
+    return arg_err("split workspace");
   if (a.n_seqs == 0) return TB_OK;
   a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
   // TMA boxes need 16-token chunks inside one block and a 16-byte aligned pool

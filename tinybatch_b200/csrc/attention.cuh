@@ -18,6 +18,7 @@ struct AttnArgs {
   const int* q_start;       // [n_seqs] first row of the sequence in q / out
   const int* q_len;         // [n_seqs]
   const int* ctx_len;       // [n_seqs]
+  const int* seq_order;     // decode: [n_seqs] dispatch order of the sequences, or null
   int n_seqs;
   float scale_log2;         // log2(e) / sqrt(head_dim)
   // decode splits
@@ -25,6 +26,7 @@ struct AttnArgs {
   int max_splits;
   float* ws_o;              // [n_seqs, n_kv, max_splits, 16, hd]
   float* ws_lse;            // [n_seqs, n_kv, max_splits, 16]
+  int* ws_count;            // [n_seqs, n_kv] split arrivals; zero between calls
   // prefill work list: pairs (seq, row tile)
   const int* work;
 };

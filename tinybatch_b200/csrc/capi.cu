@@ -101,7 +101,7 @@ size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits) {
 int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
               const float* sq, int sq_parts, int sq_ld, float inv_d, float eps, void* out,
               int ld_out, int out_f32, int bn, int splits, void* ws, size_t ws_bytes,
-              void* stream) {
+              const tb_l2_prefetch* next, void* stream) {
   if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (out == nullptr || ld_out < N || (out_f32 ? ld_out % 4 : ld_out % 8))
     return arg_err("out / ld_out");
@@ -109,6 +109,7 @@ int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int 
   g.out = out;
   g.ld_out = ld_out;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
+  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(out_f32 ? EPI_F32 : EPI_BF16, bn, x, ldx, w, ldw, g,
                      static_cast<cudaStream_t>(stream));
@@ -119,7 +120,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
                    int sq_parts, int sq_ld, float inv_d, float eps, const float* rope_cos,
                    const float* rope_sin, int max_pos, const int* positions, const int* slots,
                    void* q_out, int ld_q, void* kv_pool, int block_size, int bn, int splits,
-                   void* ws, size_t ws_bytes, void* stream) {
+                   void* ws, size_t ws_bytes, const tb_l2_prefetch* next, void* stream) {
   if (!valid_bn(bn) || head_dim <= 0 || head_dim % 16 || bn % head_dim)
     return arg_err("bn must be 64/128/192/256 and a multiple of head_dim (multiple of 16)");
   if (bias == nullptr || rope_cos == nullptr || rope_sin == nullptr || positions == nullptr ||
@@ -143,6 +144,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
   g.block_size = block_size;
   g.max_pos = max_pos;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
+  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(EPI_QKV, bn, x, ldx, w_qkv, ldw, g, static_cast<cudaStream_t>(stream));
 }
@@ -150,7 +152,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
 int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, int K,
                       int n_feat, const float* sq, int sq_parts, int sq_ld, float inv_d,
                       float eps, void* act, int ld_act, int bn, int splits, void* ws,
-                      size_t ws_bytes, void* stream) {
+                      size_t ws_bytes, const tb_l2_prefetch* next, void* stream) {
   if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (n_feat <= 0 || n_feat % 16 || ld_act < n_feat || ld_act % 8 || act == nullptr)
     return arg_err("n_feat must be a multiple of 16; act / ld_act");
@@ -161,6 +163,7 @@ int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, 
   g.ld_out = ld_act;
   g.n_feat = n_feat;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
+  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(EPI_SWIGLU, bn, x, ldx, w_gu, ldw, g, static_cast<cudaStream_t>(stream));
 }
@@ -169,7 +172,7 @@ int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M
                            float* h, int ld_h, const void* g_next, void* hg, int ld_hg,
                            float* sq_out, int sq_out_ld, const int* row_dst, void* hg2,
                            float* sq2, int sq2_ld, int bn, int splits, void* ws,
-                           size_t ws_bytes, void* stream) {
+                           size_t ws_bytes, const tb_l2_prefetch* next, void* stream) {
   if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (N % 16 || h == nullptr || g_next == nullptr || hg == nullptr || sq_out == nullptr)
     return arg_err("N must be a multiple of 16; h / g_next / hg / sq_out");
@@ -189,9 +192,17 @@ int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M
   g.sq2 = sq2;
   g.sq2_ld = sq2_ld;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
+  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(EPI_RESID, bn, x, ldx, w, ldw, g, static_cast<cudaStream_t>(stream));
 }
+
+// Split-KV workspace: a fixed 64 KiB region of arrival counters (one int per
+// (seq, kv head), at most ATTN_MAX_PAIRS pairs; zero between calls) first, so
+// the counters sit at the same offsets whatever the call's size, then the
+// per-split outputs and log-sum-exps.
+constexpr size_t ATTN_COUNTER_BYTES = 64 << 10;
+constexpr int ATTN_MAX_PAIRS = (int)(ATTN_COUNTER_BYTES / sizeof(int));
 
 size_t tb_attention_scratch_bytes(int n_seqs, int n_kv_heads, int head_dim, int max_ctx,
                                   int split_tokens) {
@@ -200,15 +211,17 @@ size_t tb_attention_scratch_bytes(int n_seqs, int n_kv_heads, int head_dim, int 
   const int splits = per > 0 ? (chunks + per - 1) / per : 0;
   if (splits <= 1) return 0;
   const size_t rows = (size_t)n_seqs * n_kv_heads * splits * 16;
-  return round_up(rows * head_dim * sizeof(float)) + round_up(rows * sizeof(float));
+  return ATTN_COUNTER_BYTES + round_up(rows * head_dim * sizeof(float)) +
+         round_up(rows * sizeof(float));
 }
 
 int tb_paged_attention_decode(const void* q, int ld_q, void* out, int ld_out,
                               const void* kv_pool, int num_blocks, int n_q_heads,
                               int n_kv_heads, int head_dim, int block_size,
                               const int* block_tables, int bt_ld, const int* q_start,
-                              const int* q_len, const int* ctx_len, int n_seqs, int max_ctx,
-                              int split_tokens, void* ws, size_t ws_bytes, void* stream) {
+                              const int* q_len, const int* ctx_len, const int* seq_order,
+                              int n_seqs, int max_ctx, int split_tokens, void* ws,
+                              size_t ws_bytes, void* stream) {
   if (split_tokens <= 0 || split_tokens % 16 || max_ctx <= 0) return arg_err("split_tokens / max_ctx");
   AttnArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -225,6 +238,7 @@ int tb_paged_attention_decode(const void* q, int ld_q, void* out, int ld_out,
   a.q_start = q_start;
   a.q_len = q_len;
   a.ctx_len = ctx_len;
+  a.seq_order = seq_order;
   a.n_seqs = n_seqs;
   a.split_chunks = split_tokens / 16;
   a.max_splits = ((max_ctx + 15) / 16 + a.split_chunks - 1) / a.split_chunks;
@@ -232,9 +246,14 @@ int tb_paged_attention_decode(const void* q, int ld_q, void* out, int ld_out,
     const size_t need = tb_attention_scratch_bytes(n_seqs, n_kv_heads, head_dim, max_ctx, split_tokens);
     if (ws == nullptr || ws_bytes < need) return arg_err("attention scratch too small");
     if (reinterpret_cast<uintptr_t>(ws) % ALIGN) return arg_err("scratch must be 256-byte aligned");
+    if ((long long)n_seqs * n_kv_heads > ATTN_MAX_PAIRS)
+      return arg_err("split-KV decode supports at most 16384 (sequence, kv head) pairs");
     const size_t rows = (size_t)n_seqs * n_kv_heads * a.max_splits * 16;
-    a.ws_o = static_cast<float*>(ws);
-    a.ws_lse = reinterpret_cast<float*>(static_cast<char*>(ws) + round_up(rows * head_dim * sizeof(float)));
+    char* base = static_cast<char*>(ws);
+    a.ws_count = reinterpret_cast<int*>(base);
+    a.ws_o = reinterpret_cast<float*>(base + ATTN_COUNTER_BYTES);
+    a.ws_lse = reinterpret_cast<float*>(base + ATTN_COUNTER_BYTES +
+                                        round_up(rows * head_dim * sizeof(float)));
   }
   return attn_decode(a, head_dim, static_cast<cudaStream_t>(stream));
 }

@@ -142,7 +142,7 @@ int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int 
                                      int ld_hg, float* sq_out, int sq_out_ld, const int* row_dst,
                                      void* hg2, float* sq2, int sq2_ld, void* comm, int site,
                                      int n_sites, int two_shot, int bn, int splits,
-                                     void* stream) {
+                                     const tb_l2_prefetch* next, void* stream) {
   CommHost* c = static_cast<CommHost*>(comm);
   if (c == nullptr || c->dev.state == nullptr) {
     set_last_error("communicator not opened");
@@ -180,6 +180,8 @@ int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int 
   g.comm.n_sites = n_sites;
   g.comm.two_shot = two_shot ? 1 : 0;
   if (c->world == 1) g.comm.world = 0;  // a single rank needs no exchange
+  int rc = gemm_set_prefetch(g, next);
+  if (rc) return rc;
   // split-K goes through the cluster (no scratch): every CTA reaches the epilogue
   return gemm_launch(EPI_RESID, bn, x, ldx, w, ldw, g, static_cast<cudaStream_t>(stream));
 }

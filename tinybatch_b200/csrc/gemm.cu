@@ -1,5 +1,6 @@
 // tcgen05 GEMM kernel and its host launcher (see gemm.cuh for the design).
 #include <stdio.h>
+#include <string.h>
 
 #include "gemm.cuh"
 #include "host.h"
@@ -16,8 +17,9 @@ enum SplitMode : int {
   SPLIT_NONE = 0,     // one CTA per tile
   SPLIT_GLOBAL = 1,   // partials in caller scratch; last CTA to arrive reduces
   SPLIT_CLUSTER = 2,  // the splits of a tile form a thread-block cluster; each
-                      // CTA parks its partial in its own shared memory and
-                      // reduces a slice of columns over DSMEM
+                      // CTA stores every 16-column chunk of its partial into
+                      // the shared memory of the chunk's owner CTA (DSMEM)
+                      // and reduces the chunks it owns locally
 };
 
 __device__ __forceinline__ void trace_at(const GemmArgs& g, int point) {
@@ -33,17 +35,110 @@ struct GemmLayout {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = STAGES * A_BYTES;
   static constexpr int OFF_BAR = OFF_B + STAGES * B_BYTES;
-  static constexpr int BAR_BYTES = (2 * STAGES + 1) * 8 + 16 + BM * 4;  // + per-row sums
+  static constexpr int BAR_BYTES = (2 * STAGES + 1) * 8 + 16 + 4 * BM * 4;  // + RowStage arrays
   static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;                // + alignment slack
-  // cluster mode parks the fp32 tile [BN/4][BM] float4 over the stage ring
-  static_assert(BN * BM * 4 <= OFF_BAR, "stage ring too small for the partial tile");
+  // cluster mode receives the members' partial chunks over the stage ring
+  static constexpr int RING = OFF_BAR;
 };
 
+// Bytes of shared memory a cluster member receives: `splits` sources, each
+// sending the ceil(np / splits) pairs of cp 16-column chunks this member owns,
+// 128 rows x 16 fp32 per chunk.
+__host__ __device__ constexpr int cluster_region_bytes(int np, int cp, int splits) {
+  return splits * ((np + splits - 1) / splits) * cp * BM * 16 * 4;
+}
+
+// Deferred RMSNorm scale of row m: rsqrt(mean of h^2 + eps) from the
+// per-part partial sums the producing kernel wrote.
 __device__ __forceinline__ float row_scale(const GemmArgs& g, int m) {
   if (g.sq == nullptr || m >= g.M) return 1.f;
   float s = 0.f;
-  for (int p = 0; p < g.sq_parts; ++p) s += g.sq[(size_t)p * g.sq_ld + m];
+  int p = 0;
+  for (; p + 8 <= g.sq_parts; p += 8) {
+    float t[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t[i] = g.sq[(size_t)(p + i) * g.sq_ld + m];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += t[i];
+  }
+  for (; p < g.sq_parts; ++p) s += g.sq[(size_t)p * g.sq_ld + m];
   return rsqrtf(s * g.inv_d + g.eps);
+}
+
+// Warm L2 with this CTA's share of a weight the next kernel streams: for
+// every (256-row block, split segment) of pf, the first pf.bytes of the
+// segment's columns, as 256 x 256 tensor boxes (128 KiB per prefetch), items
+// spread over the grid and the warp's lanes.
+__device__ __forceinline__ void prefetch_box(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+constexpr int PF_BOX = 256;
+
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, const CUtensorMap* map,
+                                                  int lane) {
+  const int num_k = (pf.k + BK - 1) / BK;
+  const int row_blocks = (pf.rows + PF_BOX - 1) / PF_BOX;
+  const int cols = pf.bytes / 2;
+  const int boxes = (cols + PF_BOX - 1) / PF_BOX;   // per (row block, segment)
+  const long long items = (long long)row_blocks * pf.splits * boxes;
+  const long long cta = blockIdx.x + (long long)blockIdx.y * gridDim.x;
+  const long long stride = (long long)gridDim.x * gridDim.y * 32;
+  for (long long it = cta * 32 + lane; it < items; it += stride) {
+    const int b = (int)(it % boxes);
+    const int z = (int)((it / boxes) % pf.splits);
+    const int rb = (int)(it / ((long long)boxes * pf.splits));
+    const int kb = (int)((long long)z * num_k / pf.splits);
+    const int ke = (int)((long long)(z + 1) * num_k / pf.splits);
+    const int x = kb * BK + b * PF_BOX;   // a multiple of 64 columns: 16-byte aligned
+    if (x >= min(ke * BK, pf.k)) continue;
+    prefetch_box(map, x, rb * PF_BOX);
+  }
+}
+
+// How a tile's columns are grouped for the epilogue and, in cluster split-K,
+// which member owns them.  The unit of work is a "pair" of cp 16-column
+// chunks that one thread finishes together: a single chunk (plain outputs,
+// residual; 16-wide heads), the gate and up chunks of the same features
+// (SwiGLU: gate columns [0, BN/2), up columns [BN/2, BN)), or the two chunks a
+// RoPE rotation mixes (QKV, head_dim >= 32: columns j and j + head_dim/2 of a
+// head).  Pair p belongs to cluster member p % splits, at slot
+// (p / splits) * cp + which of that member's receive region.
+struct TileUnits {
+  int np;    // pairs in the tile
+  int cp;    // chunks per pair: 1 or 2
+  int hc;    // paired kinds: chunks per half (SwiGLU: per tile half; QKV: per head half)
+  int kind;  // 0 single chunks, 1 SwiGLU halves, 2 RoPE halves of each head
+  __device__ __forceinline__ int chunk(int p, int which) const {
+    if (kind == 0) return p;
+    if (kind == 1) return p + which * hc;
+    return (p / hc) * 2 * hc + which * hc + p % hc;
+  }
+  __device__ __forceinline__ void pair_of(int k, int& p, int& which) const {
+    if (kind == 0) {
+      p = k;
+      which = 0;
+    } else if (kind == 1) {
+      which = k / hc;
+      p = k % hc;
+    } else {
+      const int r = k % (2 * hc);
+      which = r / hc;
+      p = (k / (2 * hc)) * hc + r % hc;
+    }
+  }
+};
+
+template <int BN, int EPI>
+__device__ __forceinline__ TileUnits tile_units(const GemmArgs& g) {
+  if constexpr (EPI == EPI_SWIGLU) return {BN / 32, 2, BN / 32, 1};
+  if constexpr (EPI == EPI_QKV) {
+    if (g.head_dim >= 32) return {BN / 32, 2, g.head_dim / 32, 2};
+  }
+  return {BN / 16, 1, 0, 0};
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
@@ -58,77 +153,102 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t smem_addr, uint32_t ran
   return r;
 }
 
-__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+// 16 bytes into the shared memory of a cluster member (a mapa address).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
   float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "r"(addr)
                : "memory");
   return v;
 }
 
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+// ------------------------------------------------------------- staging
+// A 16-column chunk of a 128-row tile in shared memory: [4 float4][BM rows],
+// chunks numbered [source][slot] (cluster split-K keeps one source per
+// member).  A warp reading TMEM (one row per thread) stores 512 contiguous
+// bytes per instruction, which also keeps its DSMEM stores dense; the
+// finisher's lanes read 8 consecutive rows per 8-lane phase (no bank
+// conflicts).
+__device__ __forceinline__ uint32_t stage_off(int src, int slot, int nslot, int row, int i) {
+  return (uint32_t)((((src * nslot + slot) * 4 + i) * BM + row) * 16);
 }
 
-// Accumulator access for the epilogue: columns [c, c+W) of this thread's row.
-// In SPLIT_NONE / SPLIT_GLOBAL mode it reads TMEM (collective over the warp:
-// every lane calls it); in SPLIT_CLUSTER mode it sums the cluster's parked
-// partial tiles in rank order.
+// Staged float4 at byte offset `off` of the CTA's shared memory (plain C++
+// accesses: independent loads pipeline; the barriers around them are
+// memory-clobbering asm, which orders them).
+__device__ __forceinline__ const float4& staged(const uint8_t* smem, uint32_t off) {
+  return *reinterpret_cast<const float4*>(smem + off);
+}
+
+// Sum over the sources of float4 i of chunk `slot`, row `row`, in source
+// order (at most 8 sources, all loads issued before the first add).
+__device__ __forceinline__ float4 stage_sum(const uint8_t* smem, int nsrc, int nslot, int slot,
+                                            int row, int i) {
+  float4 v[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s)
+    if (s < nsrc) v[s] = staged(smem, stage_off(s, slot, nslot, row, i));
+  float4 a = v[0];
+#pragma unroll
+  for (int s = 1; s < 8; ++s) {
+    if (s < nsrc) {
+      a.x += v[s].x;
+      a.y += v[s].y;
+      a.z += v[s].z;
+      a.w += v[s].w;
+    }
+  }
+  return a;
+}
+
+// Accumulator access for the epilogue: columns [16k, 16k+16) of this
+// thread's row.  In SPLIT_NONE / SPLIT_GLOBAL mode it reads TMEM (collective
+// over the warp: every lane calls it); in SPLIT_CLUSTER mode it sums, in
+// member order, the partials the cluster members stored at `slot` of this
+// CTA's receive region.
 template <int BN>
 struct AccReader {
   uint32_t taddr;   // TMEM address of this warp's lane quarter, column 0
   int mode, splits, z, row;
   const float* ws;  // SPLIT_GLOBAL: this tile's workspace, [splits][BN][128]
-  uint32_t red;     // SPLIT_CLUSTER: shared address of the parked tile
-  template <int W>
-  __device__ __forceinline__ void load(int c, float* v) const {
+  const uint8_t* smem;  // SPLIT_CLUSTER: the receive region (this CTA's shared memory)
+  int nslot;        // SPLIT_CLUSTER: chunk slots per source member
+  __device__ __forceinline__ void load16(int k, int slot, float* v) const {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.f;
     if (mode == SPLIT_CLUSTER) {
-      // ordered sum over the cluster members, the next member's loads in
-      // flight while the current one is added
-      const uint32_t off = (uint32_t)(((c / 4) * BM + row) * 16);
-      float4 cur[W / 4], nxt[W / 4];
 #pragma unroll
-      for (int i = 0; i < W / 4; ++i) cur[i] = ld_cluster_v4(cluster_map(red, 0) + off + i * BM * 16);
-#pragma unroll
-      for (int j = 0; j < W; ++j) v[j] = 0.f;
-      for (int s = 0; s < splits; ++s) {
-        if (s + 1 < splits) {
-          const uint32_t base = cluster_map(red, s + 1) + off;
-#pragma unroll
-          for (int i = 0; i < W / 4; ++i) nxt[i] = ld_cluster_v4(base + i * BM * 16);
-        }
-#pragma unroll
-        for (int i = 0; i < W / 4; ++i) {
-          v[4 * i] += cur[i].x;
-          v[4 * i + 1] += cur[i].y;
-          v[4 * i + 2] += cur[i].z;
-          v[4 * i + 3] += cur[i].w;
-          cur[i] = nxt[i];
-        }
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = stage_sum(smem, splits, nslot, slot, row, i);
+        v[4 * i] = a.x;
+        v[4 * i + 1] = a.y;
+        v[4 * i + 2] = a.z;
+        v[4 * i + 3] = a.w;
       }
       return;
     }
-    float own[W];
-    if constexpr (W == 16) tmem_ld16(taddr + c, own);
-    else tmem_ld8(taddr + c, own);
+    float own[16];
+    tmem_ld16(taddr + 16 * k, own);
     if (mode == SPLIT_NONE) {
 #pragma unroll
-      for (int j = 0; j < W; ++j) v[j] = own[j];
+      for (int j = 0; j < 16; ++j) v[j] = own[j];
       return;
     }
-#pragma unroll
-    for (int j = 0; j < W; ++j) v[j] = 0.f;
     for (int s = 0; s < splits; ++s) {
       if (s == z) {
 #pragma unroll
-        for (int j = 0; j < W; ++j) v[j] += own[j];
+        for (int j = 0; j < 16; ++j) v[j] += own[j];
       } else {
-        const float* p = ws + ((size_t)s * BN + c) * BM + row;
+        const float* p = ws + ((size_t)s * BN + 16 * k) * BM + row;
 #pragma unroll
-        for (int j = 0; j < W; ++j) v[j] += __ldcg(p + (size_t)j * BM);
+        for (int j = 0; j < 16; ++j) v[j] += __ldcg(p + (size_t)j * BM);
       }
     }
   }
@@ -317,7 +437,7 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
     const int n = tn * BN + u * 16;
     if (n >= N) break;
     float v[16];
-    acc.template load<16>(u * 16, v);
+    acc.load16(u, u / n_own, v);
     if (!valid) continue;
     if (c.two_shot) {
       put16(rs_at(n / per_owner, c.rank), u, v);
@@ -409,85 +529,37 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
   return ss;
 }
 
-// The fused epilogue for this thread's row.  Work is divided in units (a
-// 16-column chunk; a head for EPI_QKV); this CTA handles the units u with
-// u % n_own == own (all units unless the tile is split over a cluster).
-// EPI_RESID returns the row's sum of h^2 over the handled columns.
-template <int BN, int EPI>
-__device__ __forceinline__ float run_epilogue(const GemmArgs& g, const AccReader<BN>& acc, int tm,
-                                              int tn, int row, int own, int n_own,
-                                              const ResidPre& pre) {
+// This CTA's partial row sum of h^2 -> row `part` of sq_out (and of sq2 for
+// gathered rows).
+__device__ __forceinline__ void store_row_sumsq(const GemmArgs& g, int tm, int part, int row,
+                                                float ss) {
   const int m = tm * BM + row;
-  const bool valid = m < g.M;
-  const float rs = row_scale(g, m);
-  float ss = 0.f;
+  if (m >= g.M) return;
+  g.sq_out[(size_t)part * g.sq_out_ld + m] = ss;
+  if (g.row_dst != nullptr) {
+    const int dst = g.row_dst[m];
+    if (dst >= 0) g.sq2[(size_t)part * g.sq2_ld + dst] = ss;
+  }
+}
 
-  if constexpr (EPI == EPI_F32 || EPI == EPI_BF16) {
-    for (int u = own; u < BN / 16; u += n_own) {
-      const int c = u * 16;
-      const int n = tn * BN + c;
-      if (n >= g.N) break;
-      float v[16];
-      acc.template load<16>(c, v);
-      if (!valid) continue;
-      if constexpr (EPI == EPI_F32) {
-        float* o = reinterpret_cast<float*>(g.out) + (size_t)m * g.ld_out + n;
-        if (n + 16 <= g.N) {
-#pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            *reinterpret_cast<float4*>(o + j) =
-                make_float4(v[j] * rs, v[j + 1] * rs, v[j + 2] * rs, v[j + 3] * rs);
-        } else {
-          for (int j = 0; j < 16 && n + j < g.N; ++j) o[j] = v[j] * rs;
-        }
-      } else {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + n;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] *= rs;
-        if (n + 16 <= g.N) {
-          store_bf16x8(o, v);
-          store_bf16x8(o + 8, v + 8);
-        } else {
-          for (int j = 0; j < 16 && n + j < g.N; ++j) o[j] = __float2bfloat16_rn(v[j]);
-        }
-      }
-    }
-  } else if constexpr (EPI == EPI_SWIGLU) {
-    // Tile tn holds features [tn*BN/2, (tn+1)*BN/2): gate rows first, up rows second.
-    constexpr int HALF = BN / 2;
-    for (int u = own; u < HALF / 16; u += n_own) {
-      const int c = u * 16;
-      const int f = tn * HALF + c;
-      if (f >= g.n_feat) break;
-      float gv[16], uv[16];
-      acc.template load<16>(c, gv);
-      acc.template load<16>(HALF + c, uv);
-      if (!valid) continue;
-      float y[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float a = gv[j] * rs, b = uv[j] * rs;
-        y[j] = a / (1.f + __expf(-a)) * b;
-      }
-      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + f;
-      store_bf16x8(o, y);
-      store_bf16x8(o + 8, y + 8);
-    }
-  } else if constexpr (EPI == EPI_RESID) {
-    if (g.comm.world > 1) return run_resid_tp<BN>(g, acc, tm, tn, row, own, n_own, pre);
-    const int dst = (valid && g.row_dst != nullptr) ? g.row_dst[m] : -1;
-    for_resid_units<BN>(g, m, tn, own, n_own, pre,
-                        [&](int u, int n, const float* h_old, const uint32_t* g8) {
-                          float v[16];
-                          acc.template load<16>(u * 16, v);
-                          if (valid) ss += resid_update(g, m, n, dst, v, h_old, g8);
-                        });
-  } else if constexpr (EPI == EPI_QKV) {
-    const int hd = g.head_dim, half = hd >> 1;
-    const int heads_in_tile = BN / hd;
-    const int total_heads = g.n_q_heads + 2 * g.n_kv_heads;
-    int pos = 0, slot = 0;
-    if (valid) {
+// ------------------------------------------------------------ finisher
+// Per-row values of the tile, written by the epilogue warps (one row per
+// thread) before the accumulator is ready and read by the finisher.
+struct RowStage {
+  float* rs;  // deferred-norm scale
+  int* pos;   // QKV: rotary position
+  int* slot;  // QKV: KV-cache slot (-1: none)
+  int* dst;   // RESID: gathered row of hg2 / sq2 (-1: none)
+};
+
+template <int EPI>
+__device__ __forceinline__ void stage_rows(const GemmArgs& g, const RowStage& rw, int tm,
+                                           int row) {
+  const int m = tm * BM + row;
+  rw.rs[row] = row_scale(g, m);
+  if constexpr (EPI == EPI_QKV) {
+    int pos = 0, slot = -1;
+    if (m < g.M) {
       pos = g.positions[m];
       slot = g.slots[m];
       if (pos < 0 || pos >= g.max_pos || slot < 0) {
@@ -496,83 +568,356 @@ __device__ __forceinline__ float run_epilogue(const GemmArgs& g, const AccReader
         slot = -1;
       }
     }
-    const int blk = slot >= 0 ? slot / g.block_size : 0;
-    const int off = slot >= 0 ? slot % g.block_size : 0;
-    for (int hh = own; hh < heads_in_tile; hh += n_own) {
-      const int head = tn * heads_in_tile + hh;
-      if (head >= total_heads) break;
-      const int c0 = hh * hd;
-      const int n0 = head * hd;
-      __nv_bfloat16* dst;
-      bool rotate = true;
-      if (head < g.n_q_heads) {
-        dst = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + (size_t)head * hd;
-      } else {
-        const int is_v = head >= g.n_q_heads + g.n_kv_heads;
-        const int kvh = head - g.n_q_heads - (is_v ? g.n_kv_heads : 0);
-        rotate = !is_v;
-        dst = g.kv_pool +
-              ((((size_t)blk * 2 + is_v) * g.n_kv_heads + kvh) * g.block_size + off) * hd;
-      }
-      const bool store = valid && (slot >= 0 || head < g.n_q_heads);
-      if (rotate) {
-        for (int j = 0; j < half; j += 8) {
-          float lo[8], hi[8], bl[8], bh[8];
-          acc.template load<8>(c0 + j, lo);
-          acc.template load<8>(c0 + half + j, hi);
-          if (!store) continue;
-          load_bf16x8(g.bias + n0 + j, bl);
-          load_bf16x8(g.bias + n0 + half + j, bh);
-          const float* cs = g.rope_cos + (size_t)pos * half + j;
-          const float* sn = g.rope_sin + (size_t)pos * half + j;
-          float ol[8], oh[8];
+    rw.pos[row] = pos;
+    rw.slot[row] = slot;
+  }
+  if constexpr (EPI == EPI_RESID)
+    rw.dst[row] = (m < g.M && g.row_dst != nullptr) ? g.row_dst[m] : -1;
+}
+
+// Copy this CTA's accumulator (TMEM, one row per thread) into the staging
+// chunks: in cluster split-K straight into the shared memory of the member
+// that owns each chunk (source z), else into this CTA's own staging area
+// (source 0).  64 columns per TMEM load.
+template <int BN>
+__device__ __forceinline__ void stage_acc(const AccReader<BN>& acc, const TileUnits& tu, int S,
+                                          int z, uint8_t* smem, int nslot, int row,
+                                          bool cluster) {
+  const uint32_t region = smem_u32(smem);
+#pragma unroll 1
+  for (int k0 = 0; k0 < BN / 16; k0 += 4) {
+    float v[64];
+    tmem_ld64(acc.taddr + 16 * k0, v);
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const float x1 = lo[t] * rs + bl[t], x2 = hi[t] * rs + bh[t];
-            const float c = cs[t], s = sn[t];
-            ol[t] = x1 * c - x2 * s;
-            oh[t] = x2 * c + x1 * s;
-          }
-          store_bf16x8(dst + j, ol);
-          store_bf16x8(dst + half + j, oh);
-        }
-      } else {
-        for (int j = 0; j < hd; j += 8) {
-          float x[8], b[8];
-          acc.template load<8>(c0 + j, x);
-          if (!store) continue;
-          load_bf16x8(g.bias + n0 + j, b);
+    for (int kk = 0; kk < 4; ++kk) {
+      int p, which;
+      tu.pair_of(k0 + kk, p, which);
+      const int slot = (p / S) * tu.cp + which;
+      if (cluster) {
+        const uint32_t dst = cluster_map(region, (uint32_t)(p % S));
 #pragma unroll
-          for (int t = 0; t < 8; ++t) x[t] = x[t] * rs + b[t];
-          store_bf16x8(dst + j, x);
-        }
+        for (int i = 0; i < 4; ++i)
+          st_cluster_v4(dst + stage_off(z, slot, nslot, row, i), v[16 * kk + 4 * i],
+                        v[16 * kk + 4 * i + 1], v[16 * kk + 4 * i + 2], v[16 * kk + 4 * i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<float4*>(smem + stage_off(0, slot, nslot, row, i)) =
+              make_float4(v[16 * kk + 4 * i], v[16 * kk + 4 * i + 1], v[16 * kk + 4 * i + 2],
+                          v[16 * kk + 4 * i + 3]);
       }
     }
   }
-  return ss;
 }
 
-// Row sum of h^2 for the whole tile -> sq_out (and sq2 for gathered rows).
-__device__ __forceinline__ void store_row_sumsq(const GemmArgs& g, int tm, int tn, int row,
-                                                float ss) {
-  const int m = tm * BM + row;
-  if (m >= g.M) return;
-  g.sq_out[(size_t)tn * g.sq_out_ld + m] = ss;
-  if (g.row_dst != nullptr) {
-    const int dst = g.row_dst[m];
-    if (dst >= 0) g.sq2[(size_t)tn * g.sq2_ld + dst] = ss;
+// Global split-K, last CTA of a tile: own accumulator + the other splits'
+// workspace partials, summed in split order, into the staging area.
+template <int BN>
+__device__ __forceinline__ void stage_global(const AccReader<BN>& acc, const TileUnits& tu,
+                                             uint8_t* smem, int nslot, int row) {
+  for (int k = 0; k < BN / 16; ++k) {
+    float v[16];
+    acc.load16(k, 0, v);
+    int p, which;
+    tu.pair_of(k, p, which);
+    const int slot = p * tu.cp + which;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<float4*>(smem + stage_off(0, slot, nslot, row, i)) =
+          make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   }
+}
+
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+
+__device__ __forceinline__ uint2 pack_bf16x4(float a, float b, float c, float d) {
+  return make_uint2(pack_bf16x2(a, b), pack_bf16x2(c, d));
+}
+
+// Finisher thread layout: thread t (0..127), lane l = t % 32 of epilogue
+// warp w = t / 32, handles float4 i = l / 8 (columns 4i..4i+3 of a chunk) of
+// rows fin_row(t) + 32 j, j < 4, where fin_row(t) = l % 8 + 8 w: one warp
+// instruction covers 8 rows x 64 contiguous bytes of a row-major output, and
+// the 4 threads of a row are lanes l, l^8, l^16, l^24.
+__device__ __forceinline__ int fin_piece(int t) { return (t & 31) >> 3; }
+__device__ __forceinline__ int fin_row(int t) { return (t & 7) + 8 * (t >> 5); }
+//
+// Residual inputs of one chunk for a finisher thread: its 4 rows of h (4
+// float4) and 4 bf16 of g_next.  The first chunk's are loaded before the
+// accumulator is ready; every later chunk's one chunk ahead.
+struct FinPre {
+  float4 h[4];
+  uint2 g;
+};
+
+__device__ __forceinline__ void load_fin_inputs(const GemmArgs& g, int tm, int r0, int n,
+                                                FinPre& p) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int m = tm * BM + r0 + 32 * j;
+    p.h[j] = m < g.M ? *reinterpret_cast<const float4*>(g.h + (size_t)m * g.ld_h + n)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  p.g = *reinterpret_cast<const uint2*>(g.gnext + n);
+}
+
+template <int BN>
+__device__ __forceinline__ void fin_prefetch(const GemmArgs& g, int tm, int tn, int own, int t,
+                                             FinPre& p) {
+  if (own < BN / 16 && tn * BN + own * 16 < g.N)
+    load_fin_inputs(g, tm, fin_row(t), tn * BN + own * 16 + 4 * fin_piece(t), p);
+}
+
+// h += acc; hg = bf16(h * g_next) (and its copy in row dst of hg2); the
+// CTA's partial sums of h^2 per row -> row `part` of sq_out / sq2.  One
+// rolled loop over the chunks (the epilogue runs once per CTA, from a cold
+// instruction cache: compact code matters), each chunk's inputs loaded one
+// chunk ahead.
+template <int BN>
+__device__ __forceinline__ void finish_resid(const GemmArgs& g, const RowStage& rw,
+                                             const uint8_t* smem, int nsrc, int nslot, int tm,
+                                             int tn, int own, int n_own, int part, int t,
+                                             const FinPre& pre) {
+  constexpr int U = BN / 16;
+  const int i = fin_piece(t), r0 = fin_row(t);
+  float ss[4] = {0.f, 0.f, 0.f, 0.f};
+  FinPre cur = pre;
+  int lp = 0;
+#pragma unroll 1
+  for (int u = own; u < U && tn * BN + u * 16 < g.N; u += n_own, ++lp) {
+    const int un = u + n_own;
+    FinPre nxt;
+    if (un < U && tn * BN + un * 16 < g.N)
+      load_fin_inputs(g, tm, r0, tn * BN + un * 16 + 4 * i, nxt);
+    const int n = tn * BN + u * 16 + 4 * i;
+    const float2 ga = bf16x2_to_float2(cur.g.x), gb = bf16x2_to_float2(cur.g.y);
+    // all four rows' sums first: their shared-memory loads overlap
+    float4 acc4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc4[j] = stage_sum(smem, nsrc, nslot, lp, r0 + 32 * j, i);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int row = r0 + 32 * j, m = tm * BM + row;
+      if (m >= g.M) continue;
+      const float4 a = acc4[j];
+      const float4 hn = make_float4(cur.h[j].x + a.x, cur.h[j].y + a.y, cur.h[j].z + a.z,
+                                    cur.h[j].w + a.w);
+      *reinterpret_cast<float4*>(g.h + (size_t)m * g.ld_h + n) = hn;
+      ss[j] += hn.x * hn.x + hn.y * hn.y + hn.z * hn.z + hn.w * hn.w;
+      const uint2 o = pack_bf16x4(hn.x * ga.x, hn.y * ga.y, hn.z * gb.x, hn.w * gb.y);
+      *reinterpret_cast<uint2*>(g.hg + (size_t)m * g.ld_hg + n) = o;
+      const int dst = rw.dst[row];
+      if (dst >= 0) *reinterpret_cast<uint2*>(g.hg2 + (size_t)dst * g.ld_hg + n) = o;
+    }
+    if (lp == 0 && threadIdx.x == 64) trace_at(g, TR_COMBINED);
+    cur = nxt;
+  }
+  if (threadIdx.x == 64) trace_at(g, TR_BODY);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], 8);
+    ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], 16);
+  }
+  if (i == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) store_row_sumsq(g, tm, part, r0 + 32 * j, ss[j]);
+  }
+}
+
+// out = rowscale * acc, fp32 or bf16.
+template <int BN, int EPI>
+__device__ __forceinline__ void finish_linear(const GemmArgs& g, const RowStage& rw,
+                                              const uint8_t* smem, int nsrc, int nslot, int tm,
+                                              int tn, int own, int n_own, int t) {
+  const int i = fin_piece(t), r0 = fin_row(t);
+  for (int u = own, lp = 0; u < BN / 16; u += n_own, ++lp) {
+    const int n = tn * BN + u * 16 + 4 * i;
+    if (tn * BN + u * 16 >= g.N) break;
+    float4 acc4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc4[j] = stage_sum(smem, nsrc, nslot, lp, r0 + 32 * j, i);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int row = r0 + 32 * j, m = tm * BM + row;
+      if (m >= g.M) continue;
+      const float4 a = acc4[j];
+      const float rs = rw.rs[row];
+      const float v[4] = {a.x * rs, a.y * rs, a.z * rs, a.w * rs};
+      if constexpr (EPI == EPI_F32) {
+        float* o = reinterpret_cast<float*>(g.out) + (size_t)m * g.ld_out + n;
+        if (n + 4 <= g.N) *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+        else
+          for (int e = 0; e < 4 && n + e < g.N; ++e) o[e] = v[e];
+      } else {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + n;
+        if (n + 4 <= g.N) *reinterpret_cast<uint2*>(o) = pack_bf16x4(v[0], v[1], v[2], v[3]);
+        else
+          for (int e = 0; e < 4 && n + e < g.N; ++e) o[e] = __float2bfloat16_rn(v[e]);
+      }
+    }
+  }
+}
+
+// act = silu(gate) * up: the tile's first BN/2 columns are the gate rows of
+// features [tn*BN/2, (tn+1)*BN/2), the last BN/2 the matching up rows.
+template <int BN>
+__device__ __forceinline__ void finish_swiglu(const GemmArgs& g, const RowStage& rw,
+                                              const uint8_t* smem, int nsrc, int nslot, int tm,
+                                              int tn, int own, int n_own, int t) {
+  const int i = fin_piece(t), r0 = fin_row(t);
+  for (int p = own, lp = 0; p < BN / 32; p += n_own, ++lp) {
+    const int f0 = tn * (BN / 2) + p * 16;
+    if (f0 >= g.n_feat) break;
+    float4 ga4[4], ua4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ga4[j] = stage_sum(smem, nsrc, nslot, 2 * lp, r0 + 32 * j, i);
+      ua4[j] = stage_sum(smem, nsrc, nslot, 2 * lp + 1, r0 + 32 * j, i);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int row = r0 + 32 * j, m = tm * BM + row;
+      if (m >= g.M) continue;
+      const float4 a = ga4[j], b = ua4[j];
+      const float rs = rw.rs[row];
+      const float gv[4] = {a.x * rs, a.y * rs, a.z * rs, a.w * rs};
+      const float uv[4] = {b.x * rs, b.y * rs, b.z * rs, b.w * rs};
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = gv[e] / (1.f + __expf(-gv[e])) * uv[e];
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out +
+                                f0 + 4 * i) = pack_bf16x4(y[0], y[1], y[2], y[3]);
+    }
+  }
+}
+
+// Bias + RoPE of the q and k heads (bias only for v), q to q_out, k and v to
+// the paged KV pool at each row's slot.  head_dim >= 32: a pair holds 16
+// columns of a head's first half and their rotary partners half a head
+// later; head_dim 16: a pair is one head, whose halves sit with threads i
+// and i ^ 2.
+template <int BN>
+__device__ __forceinline__ void finish_qkv(const GemmArgs& g, const RowStage& rw, const uint8_t* smem,
+                                           int nsrc, int nslot, int tm, int tn, int own,
+                                           int n_own, int t) {
+  const int i = fin_piece(t), r0 = fin_row(t);
+  const int hd = g.head_dim, half = hd >> 1;
+  const int heads_in_tile = BN / hd;
+  const int total_heads = g.n_q_heads + 2 * g.n_kv_heads;
+  const TileUnits tu = tile_units<BN, EPI_QKV>(g);
+  const int per_head = tu.kind == 2 ? tu.hc : 1;
+  for (int p = own, lp = 0; p < tu.np; p += n_own, ++lp) {
+    const int hh = p / per_head, jj = p % per_head;
+    const int head = tn * heads_in_tile + hh;
+    if (hh >= heads_in_tile || head >= total_heads) break;
+    const int n0 = head * hd;
+    const bool is_q = head < g.n_q_heads;
+    const int is_v = head >= g.n_q_heads + g.n_kv_heads;
+    const int kvh = is_q ? 0 : head - g.n_q_heads - (is_v ? g.n_kv_heads : 0);
+    const bool rotate = !is_v;
+    auto dst_of = [&](int m, int kslot) -> __nv_bfloat16* {
+      if (is_q) return reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ld_out + n0;
+      const int blk = kslot / g.block_size, off = kslot % g.block_size;
+      return g.kv_pool + ((((size_t)blk * 2 + is_v) * g.n_kv_heads + kvh) * g.block_size + off) * hd;
+    };
+    if (tu.kind == 2) {
+      const int c_lo = jj * 16 + 4 * i, c_hi = half + c_lo;
+      const uint2 bl2 = *reinterpret_cast<const uint2*>(g.bias + n0 + c_lo);
+      const uint2 bh2 = *reinterpret_cast<const uint2*>(g.bias + n0 + c_hi);
+      const float2 bl0 = bf16x2_to_float2(bl2.x), bl1 = bf16x2_to_float2(bl2.y);
+      const float2 bh0 = bf16x2_to_float2(bh2.x), bh1 = bf16x2_to_float2(bh2.y);
+      const float bl[4] = {bl0.x, bl0.y, bl1.x, bl1.y}, bh[4] = {bh0.x, bh0.y, bh1.x, bh1.y};
+      float4 lo4[4], hi4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo4[j] = stage_sum(smem, nsrc, nslot, 2 * lp, r0 + 32 * j, i);
+        hi4[j] = stage_sum(smem, nsrc, nslot, 2 * lp + 1, r0 + 32 * j, i);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int row = r0 + 32 * j, m = tm * BM + row;
+        if (m >= g.M) continue;
+        const int kslot = rw.slot[row];
+        if (!is_q && kslot < 0) continue;
+        const float4 a = lo4[j], b = hi4[j];
+        const float rs = rw.rs[row];
+        const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+        float o1[4], o2[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x1 = av[e] * rs + bl[e], x2 = bv[e] * rs + bh[e];
+          if (rotate) {
+            const size_t f = (size_t)rw.pos[row] * half + c_lo + e;
+            const float c = g.rope_cos[f], s = g.rope_sin[f];
+            o1[e] = x1 * c - x2 * s;
+            o2[e] = x2 * c + x1 * s;
+          } else {
+            o1[e] = x1;
+            o2[e] = x2;
+          }
+        }
+        __nv_bfloat16* d = dst_of(m, kslot);
+        *reinterpret_cast<uint2*>(d + c_lo) = pack_bf16x4(o1[0], o1[1], o1[2], o1[3]);
+        *reinterpret_cast<uint2*>(d + c_hi) = pack_bf16x4(o2[0], o2[1], o2[2], o2[3]);
+      }
+    } else {
+      const int c = 4 * i;
+      const uint2 b2 = *reinterpret_cast<const uint2*>(g.bias + n0 + c);
+      const float2 b0 = bf16x2_to_float2(b2.x), b1 = bf16x2_to_float2(b2.y);
+      const float bias4[4] = {b0.x, b0.y, b1.x, b1.y};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int row = r0 + 32 * j, m = tm * BM + row;
+        const float4 a = stage_sum(smem, nsrc, nslot, lp, row, i);
+        const float rs = rw.rs[row];
+        const float av[4] = {a.x, a.y, a.z, a.w};
+        float x[4], o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = av[e] * rs + bias4[e];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);   // thread of piece i ^ 2
+          if (rotate) {
+            const size_t f = (size_t)rw.pos[row] * half + (i & 1) * 4 + e;
+            const float cs = g.rope_cos[f], sn = g.rope_sin[f];
+            o[e] = i < 2 ? x[e] * cs - partner * sn : x[e] * cs + partner * sn;
+          } else {
+            o[e] = x[e];
+          }
+        }
+        const int kslot = rw.slot[row];
+        if (m < g.M && (is_q || kslot >= 0))
+          *reinterpret_cast<uint2*>(dst_of(m, kslot) + c) = pack_bf16x4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void finish(const GemmArgs& g, const RowStage& rw, const uint8_t* smem,
+                                       int nsrc, int nslot, int tm, int tn, int own, int n_own,
+                                       int part, int t, const FinPre& pre) {
+  if constexpr (EPI == EPI_RESID)
+    finish_resid<BN>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, part, t, pre);
+  else if constexpr (EPI == EPI_SWIGLU)
+    finish_swiglu<BN>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, t);
+  else if constexpr (EPI == EPI_QKV)
+    finish_qkv<BN>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, t);
+  else
+    finish_linear<BN, EPI>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, t);
 }
 
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
-                   const __grid_constant__ CUtensorMap tma_b, const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_pf, const GemmArgs g) {
   using L = GemmLayout<BN, STAGES>;
   constexpr uint32_t TCOLS = tmem_cols(BN);
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint8_t* sA = smem + L::OFF_A;
   uint8_t* sB = smem + L::OFF_B;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -580,7 +925,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* done = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  float* row_ss = reinterpret_cast<float*>(tmem_slot + 4);  // [BM] per-row partial sums
+  float* row_rs = reinterpret_cast<float*>(tmem_slot + 4);  // [BM] per-row values (RowStage)
+  int* row_pos = reinterpret_cast<int*>(row_rs + BM);
+  int* row_slot = row_pos + BM;
+  int* row_dst = row_slot + BM;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mode = g.splits == 1 ? SPLIT_NONE : (g.ws != nullptr ? SPLIT_GLOBAL : SPLIT_CLUSTER);
@@ -664,7 +1012,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncwarp();
 
   const int q = warp & 3;
-  const int row = q * 32 + lane;
+  const int row = q * 32 + lane;   // TMEM lane of this thread (epilogue warps)
+  const int t = threadIdx.x - 64;  // finisher thread index (epilogue warps)
+  const TileUnits tu = tile_units<BN, EPI>(g);
+  const int S = mode == SPLIT_CLUSTER ? g.splits : 1;
+  const int nslot = ((tu.np + S - 1) / S) * tu.cp;
+  // the row-parallel projection across tensor-parallel ranks keeps one row
+  // per thread end to end (its exchange layout is row-major per thread)
+  const bool tp = EPI == EPI_RESID && g.comm.world > 1;
   AccReader<BN> acc;
   acc.taddr = tmem_base + ((uint32_t)(q * 32) << 16);
   acc.mode = mode;
@@ -672,57 +1027,47 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   acc.z = z;
   acc.row = row;
   acc.ws = nullptr;
-  acc.red = smem_u32(smem);
+  acc.smem = smem;
+  acc.nslot = nslot;
+  const RowStage rw{row_rs, row_pos, row_slot, row_dst};
 
-  ResidPre pre;
+  ResidPre pre;     // tensor-parallel residual: one row per thread
+  FinPre fpre;      // finisher: first chunk of each of its rows
   if (warp >= 2) {
     pdl_wait();   // the epilogue reads and writes buffers earlier kernels use
+    // inputs that do not depend on the accumulator load under the main loop
+    stage_rows<EPI>(g, rw, tm, row);
     if constexpr (EPI == EPI_RESID) {
-      if (mode == SPLIT_CLUSTER) resid_prefetch<BN>(g, tm, tn, row, z, g.splits, pre);
-      else resid_prefetch<BN>(g, tm, tn, row, 0, 1, pre);
+      if (tp) resid_prefetch<BN>(g, tm, tn, row, mode == SPLIT_CLUSTER ? z : 0, S, pre);
+      else fin_prefetch<BN>(g, tm, tn, mode == SPLIT_CLUSTER ? z : 0, t, fpre);
     }
   }
   if (mode == SPLIT_CLUSTER) {
-    // 1. park this CTA's fp32 partial over its (idle) stage ring as
-    //    float4 [BN/4][BM]; every MMA and TMA write has completed once
-    //    `done` fires, so the ring is free
     if (warp >= 2) {
       mbar_wait(done, 0);
       tc_fence_after();
       if (threadIdx.x == 64) trace_at(g, TR_ACC_READY);
-      float4* red = reinterpret_cast<float4*>(smem);
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(acc.taddr + c, v);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          red[(c / 4 + i) * BM + row] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      }
+    }
+    // 1. every member's MMAs are complete, so every stage ring is free
+    cluster_sync_all();
+    // 2. store each 16-column chunk of this partial into its owner's ring
+    if (warp >= 2) {
+      stage_acc<BN>(acc, tu, S, z, smem, nslot, row, true);
       if (threadIdx.x == 64) trace_at(g, TR_PARKED);
     }
+    // 3. every chunk has arrived; from here on each CTA reads only its own
+    //    shared memory, so members may exit independently
     cluster_sync_all();
     if (threadIdx.x == 64) trace_at(g, TR_CLUSTER_SYNC);
-    // 2. reduce this CTA's share of the columns across the cluster and run
-    //    the epilogue on it
-    float ss = 0.f;
-    if (warp >= 2) ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, z, g.splits, pre);
-    if constexpr (EPI == EPI_RESID) {
-      if (warp >= 2) row_ss[row] = ss;
-    }
-    if (threadIdx.x == 64) trace_at(g, TR_BODY);
-    cluster_sync_all();
-    // 3. rank 0 of the cluster combines the per-row sums of h^2
-    if constexpr (EPI == EPI_RESID) {
-      if (warp >= 2 && z == 0) {
-        float tot = 0.f;
-        const uint32_t a = smem_u32(row_ss + row);
-        for (int s = 0; s < g.splits; ++s) tot += ld_cluster_f32(cluster_map(a, s));
-        store_row_sumsq(g, tm, tn, row, tot);
+    if (warp >= 2) {
+      if (tp) {
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, z, S, pre);
+        store_row_sumsq(g, tm, tn * S + z, row, ss);
+      } else {
+        finish<BN, EPI>(g, rw, smem, S, nslot, tm, tn, z, S, tn * S + z, t, fpre);
       }
+      if (threadIdx.x == 64) trace_at(g, TR_END);
     }
-    if (threadIdx.x == 64) trace_at(g, TR_COMBINED);
-    cluster_sync_all();
-    if (threadIdx.x == 64) trace_at(g, TR_END);
   } else if (warp >= 2) {
     mbar_wait(done, 0);
     tc_fence_after();
@@ -752,10 +1097,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       acc.ws = ws_tile;
     }
     if (run) {
-      const float ss = run_epilogue<BN, EPI>(g, acc, tm, tn, row, 0, 1, pre);
-      if constexpr (EPI == EPI_RESID) store_row_sumsq(g, tm, tn, row, ss);
+      if (tp) {
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre);
+        store_row_sumsq(g, tm, tn, row, ss);
+      } else {
+        if (mode == SPLIT_GLOBAL) stage_global<BN>(acc, tu, smem, nslot, row);
+        else stage_acc<BN>(acc, tu, 1, 0, smem, nslot, row, false);
+        epi_bar();   // staged chunks and per-row values visible to every finisher thread
+        finish<BN, EPI>(g, rw, smem, 1, nslot, tm, tn, 0, 1, tn, t, fpre);
+      }
     }
     if (threadIdx.x == 64) trace_at(g, TR_END);
+  }
+  // warp 0: warm L2 with the next kernel's weights while this CTA finishes
+  if (warp == 0 && g.pf.base != nullptr) {
+    if (mode == SPLIT_CLUSTER || mbar_wait(done, 0)) l2_prefetch_share(g.pf, &tma_pf, lane);
   }
 
   tc_fence_before();
@@ -769,8 +1125,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // ------------------------------------------------------------------ host side
 
 template <int BN, int STAGES, int EPI>
-static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const GemmArgs& g,
-                     cudaStream_t stream) {
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const CUtensorMap& tpf,
+                     const GemmArgs& g, cudaStream_t stream) {
   using L = GemmLayout<BN, STAGES>;
   auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
   static bool attr_set = false;
@@ -780,21 +1136,26 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const GemmAr
     attr_set = true;
   }
   const int tiles = g.tiles_m * g.tiles_n;
-  if (g.splits > 1 && g.ws == nullptr)  // cluster split-K: a tile's splits are one cluster along x
+  if (g.splits > 1 && g.ws == nullptr) {  // cluster split-K: a tile's splits are one cluster along x
+    const bool paired = EPI == EPI_SWIGLU || (EPI == EPI_QKV && g.head_dim >= 32);
+    const int np = paired ? BN / 32 : BN / 16, cp = paired ? 2 : 1;
+    if (cluster_region_bytes(np, cp, g.splits) > L::RING)
+      return arg_err("cluster split-K: the partial chunks of this (bn, splits) do not fit shared memory");
     return launch_pdl(kern, dim3(tiles * g.splits), dim3(GEMM_THREADS), L::SMEM, stream,
-                      g.splits, "gemm cluster launch", ta, tb_, g);
+                      g.splits, "gemm cluster launch", ta, tb_, tpf, g);
+  }
   return launch_pdl(kern, dim3(tiles, g.splits), dim3(GEMM_THREADS), L::SMEM, stream, 1,
-                    "gemm launch", ta, tb_, g);
+                    "gemm launch", ta, tb_, tpf, g);
 }
 
 template <int EPI>
-static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_, const GemmArgs& g,
-                      cudaStream_t stream) {
+static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_,
+                      const CUtensorMap& tpf, const GemmArgs& g, cudaStream_t stream) {
   switch (bn) {
-    case 64: return launch_bn<64, 8, EPI>(ta, tb_, g, stream);
-    case 128: return launch_bn<128, 6, EPI>(ta, tb_, g, stream);
-    case 192: return launch_bn<192, 5, EPI>(ta, tb_, g, stream);
-    case 256: return launch_bn<256, 4, EPI>(ta, tb_, g, stream);
+    case 64: return launch_bn<64, 8, EPI>(ta, tb_, tpf, g, stream);
+    case 128: return launch_bn<128, 6, EPI>(ta, tb_, tpf, g, stream);
+    case 192: return launch_bn<192, 5, EPI>(ta, tb_, tpf, g, stream);
+    case 256: return launch_bn<256, 4, EPI>(ta, tb_, tpf, g, stream);
     default: return arg_err("bn must be 64, 128, 192 or 256");
   }
 }
@@ -831,6 +1192,22 @@ int gemm_max_active_clusters(int bn, int cluster, int* out) {
 
 unsigned long long* g_debug_trace = nullptr;
 
+int gemm_set_prefetch(GemmArgs& g, const tb_l2_prefetch* p) {
+  g.pf = L2Prefetch{};
+  if (p == nullptr || p->base == nullptr) return TB_OK;
+  if (reinterpret_cast<uintptr_t>(p->base) % 16 || p->ld % 8 || p->bytes % 16 || p->rows <= 0 ||
+      p->k <= 0 || p->ld < p->k || p->splits < 1 || p->bytes < 0)
+    return arg_err("l2 prefetch: base 16-byte aligned, ld >= k and a multiple of 8, "
+                   "bytes a multiple of 16, rows/k/splits positive");
+  g.pf.base = static_cast<const char*>(p->base);
+  g.pf.ld = p->ld;
+  g.pf.rows = p->rows;
+  g.pf.k = p->k;
+  g.pf.splits = p->splits;
+  g.pf.bytes = p->bytes;
+  return TB_OK;
+}
+
 int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb, GemmArgs g,
                 cudaStream_t stream) {
   g.trace = g_debug_trace;
@@ -853,12 +1230,24 @@ int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb,
   if (rc) return rc;
   rc = make_tmap_2d(&tbm, B, g.K, g.N, (uint64_t)ldb * 2, BK, bn);
   if (rc) return rc;
+  // L2 warm-up map of the next weight: unswizzled 256 x 256 boxes
+  CUtensorMap tpf;
+  memset(&tpf, 0, sizeof(tpf));
+  if (g.pf.base != nullptr) {
+    const uint32_t bc = (uint32_t)min(PF_BOX, g.pf.k / 8 * 8), br = (uint32_t)min(PF_BOX, g.pf.rows);
+    if (bc < 8 || g.pf.bytes < 16) {
+      g.pf = L2Prefetch{};
+    } else {
+      rc = make_tmap_2d(&tpf, g.pf.base, g.pf.k, g.pf.rows, (uint64_t)g.pf.ld * 2, bc, br, false);
+      if (rc) return rc;
+    }
+  }
   switch (epi) {
-    case EPI_F32: return launch_epi<EPI_F32>(bn, ta, tbm, g, stream);
-    case EPI_BF16: return launch_epi<EPI_BF16>(bn, ta, tbm, g, stream);
-    case EPI_QKV: return launch_epi<EPI_QKV>(bn, ta, tbm, g, stream);
-    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(bn, ta, tbm, g, stream);
-    case EPI_RESID: return launch_epi<EPI_RESID>(bn, ta, tbm, g, stream);
+    case EPI_F32: return launch_epi<EPI_F32>(bn, ta, tbm, tpf, g, stream);
+    case EPI_BF16: return launch_epi<EPI_BF16>(bn, ta, tbm, tpf, g, stream);
+    case EPI_QKV: return launch_epi<EPI_QKV>(bn, ta, tbm, tpf, g, stream);
+    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(bn, ta, tbm, tpf, g, stream);
+    case EPI_RESID: return launch_epi<EPI_RESID>(bn, ta, tbm, tpf, g, stream);
     default: return arg_err("unknown epilogue");
   }
 }

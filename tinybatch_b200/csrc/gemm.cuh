@@ -13,11 +13,16 @@
 //   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (warp w reads
 //               TMEM lanes 32*(w%4)..+31, one output row per thread), then
 //               the fused op of the GemmArgs kind below
-// With split-K each CTA writes its fp32 partial to the caller's workspace;
-// the last CTA of a tile to arrive (per-tile arrival counter) sums the
-// partials in split order (deterministic) and runs the epilogue.
+// Split-K runs in one of two forms.  Cluster (default): the splits of a tile
+// form a thread-block cluster; each member stores every 16-column chunk of
+// its fp32 partial into the shared memory of the member that owns the chunk,
+// and each owner sums its chunks in member order (deterministic) and runs the
+// epilogue on them.  Global (caller scratch): each CTA writes its partial to
+// the workspace; the last CTA of a tile to arrive (per-tile arrival counter)
+// sums the partials in split order and runs the epilogue.
 #pragma once
 
+#include "../../include/tinybatch_b200.h"
 #include "common.cuh"
 
 namespace tb {
@@ -55,6 +60,17 @@ struct CommDev {
   uint32_t* flags[TB_MAX_RANKS];
 };
 
+// An L2 warm-up request for the weight the next kernel streams: a bf16
+// matrix [rows, k] with row pitch ld elements, read by `splits` K segments
+// (split-K boundaries of 64-column blocks); the first `bytes` of every
+// (row, segment) are prefetched, in 256 x 256 tensor boxes (the kernel's
+// third tensor map).  base == nullptr: none.
+struct L2Prefetch {
+  const char* base;
+  long long ld;
+  int rows, k, splits, bytes;
+};
+
 struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n, splits, group_m;
@@ -83,7 +99,7 @@ struct GemmArgs {
   const __nv_bfloat16* gnext;
   __nv_bfloat16* hg;
   int ld_hg;
-  float* sq_out;           // [tiles_n, sq_out_ld]
+  float* sq_out;           // [parts, sq_out_ld]: tiles_n parts, tiles_n * splits in cluster split-K
   int sq_out_ld;
   const int* row_dst;      // optional: row m also written to row row_dst[m] of hg2/sq2
   __nv_bfloat16* hg2;
@@ -95,6 +111,8 @@ struct GemmArgs {
   CommDev comm;
   // debug timeline (tb_debug_trace): per CTA 16 globaltimer stamps, or null
   unsigned long long* trace;
+  // issued by warp 0 once this CTA's main loop is done
+  L2Prefetch pf;
 };
 
 // Timeline points recorded when GemmArgs::trace is set.
@@ -106,11 +124,14 @@ enum TracePoint : int {
   TR_PARTNERS,        // partner flags observed (all-reduce)
   TR_SUMS,            // reduced sums delivered (two-shot)
   TR_END,             // epilogue done
-  TR_PARKED,          // cluster split: partial parked in shared memory
-  TR_CLUSTER_SYNC,    // cluster split: every member parked
-  TR_BODY,            // cluster split: reduction + epilogue body done
-  TR_COMBINED,        // cluster split: row sums combined
+  TR_PARKED,          // cluster split: partial chunks stored to their owners
+  TR_CLUSTER_SYNC,    // cluster split: every member's chunks arrived
+  TR_BODY,            // residual finisher: every chunk updated (warp 2)
+  TR_COMBINED,        // residual finisher: first chunk updated (warp 2)
   TR_POINTS = 16,
 };
+
+// Host side (gemm.cu): validate and copy an L2 warm-up request into g.
+int gemm_set_prefetch(GemmArgs& g, const tb_l2_prefetch* p);
 
 }  // namespace tb

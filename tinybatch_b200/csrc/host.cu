@@ -48,7 +48,8 @@ static EncodeTiledFn encode_fn() {
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
-                 uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_rows) {
+                 uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_rows,
+                 bool swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) {
     set_last_error("cuTensorMapEncodeTiled entry point unavailable");
@@ -59,7 +60,8 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ro
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_last_error("cuTensorMapEncodeTiled failed (%d): inner=%llu rows=%llu pitch=%llu box=%ux%u",

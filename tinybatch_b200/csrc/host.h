@@ -21,9 +21,11 @@ int arg_err(const char* what);
 void set_last_error(const char* fmt, ...);
 
 // 2-D bf16 tensor map over a row-major [rows, inner] matrix with the given
-// row pitch, box {box_inner, box_rows}, 128-byte swizzle, zero OOB fill.
+// row pitch, box {box_inner, box_rows}, 128-byte swizzle (or none, for maps
+// only used to prefetch), zero OOB fill.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
-                 uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_rows);
+                 uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_rows,
+                 bool swizzle = true);
 
 // Launch `kern` on `stream` with programmatic stream serialisation (PDL) and,
 // when cluster_x > 1, a (cluster_x, 1, 1) thread-block cluster.

@@ -1,0 +1,164 @@
+"""Per-kernel device times of one decode step at the benchmark's shapes, and
+the small case the ncu captures run on.
+
+    python -m tinybatch_b200.kernelbench [--tp T] [--layers L] [--reps R]
+
+Workload: the Qwen2.5-14B layer shapes (d 5120, 40 q / 8 kv heads, hd 128,
+ff 13824, vocab 152064) cut to ``L`` decoder layers (default 1) and sharded
+as rank 0 of a ``T``-way tensor-parallel group (no exchange: the row-parallel
+launches run their single-rank form), random bf16 weights (seed 3); 128
+sequences decoding one token each with the benchmark's context lengths
+(prompt lengths uniform in [128, 2048], seed 3, plus 8 generated tokens),
+block size 16, each sequence's blocks contiguous in the pool.  About 4 GB on
+the device at L = 1, so a profiler can replay any launch.
+
+Every repetition queues one eager forward behind a sleep kernel (so the
+events around each launch time the kernel, not the host) and records, per
+launch kind, the device time, the algorithmic HBM bytes and the flops the
+runtime attributes to it.  Printed per kind (JSON, one line each): launches
+per step, microseconds per launch (median over repetitions), achieved GB/s
+and TFLOP/s, and the fraction of the roofline
+
+    T_roof = max(bytes / HBM copy bandwidth, flops / bf16 GEMM rate)
+
+with the burst figures of MEASURED_PEAKS.json (a copy and a cuBLAS GEMM
+measured on this pool's B200s).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+
+import torch
+
+from . import _native
+from .config import named_config
+from .model import Qwen2Paged
+from .weights import synthetic_weights
+
+N_SEQ = 128
+BLOCK = 16
+SEED = 3
+
+
+def peaks() -> tuple[dict, str]:
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    path = os.path.join(root, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def context_lengths(n: int = N_SEQ, generated: int = 8) -> list[int]:
+    """The benchmark's prompt lengths (same generator, same draws) plus the
+    tokens generated so far."""
+    rng = random.Random(SEED)
+    return [rng.randint(128, 2048) + generated for _ in range(n)]
+
+
+def build(tp: int, layers: int, device: torch.device):
+    cfg = named_config("qwen2.5-14b", n_layers=layers)
+    w = synthetic_weights(cfg, SEED, dtype=torch.bfloat16, device=device)
+    model = Qwen2Paged.from_weights(cfg, w, device=device, rank=0, world=tp, comm=None,
+                                    max_tokens=N_SEQ, max_seqs=N_SEQ)
+    del w
+    torch.cuda.empty_cache()
+    ctx = context_lengths()
+    tables, nb = [], 0
+    for c in ctx:
+        k = -(-c // BLOCK)
+        tables.append(list(range(nb, nb + k)))
+        nb += k
+    cache = model.make_kv_cache(nb, BLOCK)
+    g = torch.Generator(device=device).manual_seed(SEED)
+    for pool in cache.pools:
+        pool.copy_(torch.randn(pool.shape, generator=g, device=device).mul_(0.5))
+    ids = torch.randint(0, cfg.vocab_size, (N_SEQ,), generator=torch.Generator().manual_seed(SEED))
+    md = model.metadata(ids.tolist(), [c - 1 for c in ctx], [(i, i + 1) for i in range(N_SEQ)],
+                        tables, ctx, BLOCK)
+    return cfg, model, cache, md
+
+
+def run(tp: int = 1, layers: int = 1, reps: int = 5, l2_mb: float | None = None,
+        split_tokens: int | None = None) -> list[dict]:
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg, model, cache, md = build(tp, layers, dev)
+    if l2_mb is not None:
+        model.dm.l2_prefetch_bytes = int(l2_mb * (1 << 20))
+    model.dm.split_tokens = split_tokens
+    for _ in range(2):
+        model.forward_meta(md, cache, sample=True)
+    torch.cuda.synchronize()
+    _native.raise_on_status("kernelbench warm-up")
+    times: dict[str, list[float]] = {}
+    meta: dict[str, tuple[int, float, float]] = {}
+    for _ in range(reps):
+        torch.cuda._sleep(50_000_000)
+        model.dm.prof = []
+        model.forward_meta(md, cache, sample=True)
+        torch.cuda.synchronize()
+        per: dict[str, list] = {}
+        for kind, s, e, nbytes, flops in model.dm.prof:
+            per.setdefault(kind, []).append((s.elapsed_time(e) * 1e3, nbytes, flops))
+        for kind, lst in per.items():
+            times.setdefault(kind, []).append(sum(t for t, _, _ in lst) / len(lst))
+            meta[kind] = (len(lst), sum(b for _, b, _ in lst) / len(lst),
+                          sum(f for _, _, f in lst) / len(lst))
+        model.dm.prof = None
+    # the whole forward, launches back to back (no events between them)
+    fwd = []
+    for _ in range(reps):
+        torch.cuda._sleep(50_000_000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        model.forward_meta(md, cache, sample=True)
+        e1.record()
+        torch.cuda.synchronize()
+        fwd.append(e0.elapsed_time(e1) * 1e3)
+    _native.raise_on_status("kernelbench")
+    pk, src = peaks()
+    rows = [{"kernel": "forward", "tp": tp, "layers": layers,
+             "l2_prefetch_mb": model.dm.l2_prefetch_bytes >> 20,
+             "split_tokens": split_tokens or "auto", "launches_per_step": 1,
+             "us_per_launch": round(statistics.median(fwd), 2)}]
+    for kind, ts in times.items():
+        n, nbytes, flops = meta[kind]
+        us = statistics.median(ts)
+        t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
+        t_tc = flops / (pk["bf16_tflops"] * 1e12)
+        bound = "hbm" if t_hbm >= t_tc else "tensor"
+        rows.append({"kernel": kind, "tp": tp, "l2_prefetch_mb": model.dm.l2_prefetch_bytes >> 20,
+                     "launches_per_step": n, "us_per_launch": round(us, 2),
+                     "bytes_per_launch": int(nbytes), "GBps": round(nbytes / us / 1e3, 1),
+                     "TFLOPs": round(flops / us / 1e6, 1), "bound": bound,
+                     "us_roofline": round(max(t_hbm, t_tc) * 1e6, 2),
+                     "frac": round(max(t_hbm, t_tc) * 1e6 / us, 3), "peaks": src})
+    rows.sort(key=lambda r: -r["us_per_launch"] * r["launches_per_step"])
+    return rows
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tp", type=int, default=1, help="shard as rank 0 of this many ranks")
+    ap.add_argument("--layers", type=int, default=1)
+    ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--l2-mb", default=None,
+                    help="MiB of the next weight warmed into L2 per GEMM; comma list to sweep")
+    ap.add_argument("--split-tokens", default=None,
+                    help="decode split-KV size (default: the runtime's policy); comma list")
+    args = ap.parse_args()
+    sweep = [None] if args.l2_mb is None else [float(v) for v in args.l2_mb.split(",")]
+    splits = [None] if args.split_tokens is None else [int(v) or None for v in
+                                                       args.split_tokens.split(",")]
+    for mb in sweep:
+        for st in splits:
+            for r in run(args.tp, args.layers, args.reps, mb, st):
+                print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()

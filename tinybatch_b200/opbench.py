@@ -99,7 +99,7 @@ def run(ms: list[int], shapes=SHAPES, reps: int = 20, two_shot: bool | None = No
             h = torch.randn(M, N, generator=g, device=dev)
             hg = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             bn, splits = plan_gemm(M, N, kt)
-            sq = torch.empty(-(-N // bn), M, device=dev)
+            sq = torch.empty(ops.row_parts(N, bn, splits), M, device=dev)
 
             def plain(i):
                 ops.row_linear_residual(x, w, h, gn, hg, sq, bn=bn, splits=splits)

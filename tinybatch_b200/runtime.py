@@ -25,6 +25,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from . import _native as N
 from . import ops
 from .config import ModelConfig
 
@@ -49,7 +50,21 @@ def _cluster_capacity() -> list[int]:
     return _CLUSTERS
 
 
-def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int = 8) -> tuple[int, int]:
+# Shared-memory ring of each tile width (stages x (A + B) bytes); cluster
+# split-K receives the members' partial chunks in it.
+_RING_BYTES = {64: 8 * (16384 + 8192), 128: 6 * (16384 + 16384), 192: 5 * (16384 + 24576),
+               256: 4 * (16384 + 32768)}
+
+
+def cluster_fits(bn: int, splits: int, paired: bool = False) -> bool:
+    """Whether a cluster member's share of the partial chunks fits its ring:
+    splits x ceil(pairs / splits) x chunks-per-pair x (128 x 16 fp32)."""
+    np_, cp = (bn // 32, 2) if paired else (bn // 16, 1)
+    return splits * -(-np_ // splits) * cp * 8192 <= _RING_BYTES[bn]
+
+
+def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int = 8,
+              paired: bool = False) -> tuple[int, int]:
     """Tile width and cluster split-K factor for C[M,N] = A[M,K] B[N,K]^T.
 
     Time model (fitted to B200 measurements of the decode shapes): a CTA
@@ -57,7 +72,9 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
     min(50 GB/s, 6 TB/s / active CTAs) or is bound by its share of the
     tensor pipe (~10.8 TFLOP/s per SM); ~1 us of epilogue and 0.25 us per
     extra cluster member for the DSMEM reduction.  A launch with more CTAs
-    than fit at once runs (CTAs / resident CTAs) waves of fully busy SMs."""
+    than fit at once runs (CTAs / resident CTAs) waves of fully busy SMs.
+    ``paired``: the epilogue finishes chunk pairs (SwiGLU, RoPE); only
+    (bn, splits) whose cluster chunks fit shared memory are considered."""
     cap = _cluster_capacity()
     tm = -(-M // 128)
     num_k = -(-K // 64)
@@ -67,6 +84,8 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
         for s in range(1, max_splits + 1):
             if s > num_k or (s > 1 and num_k / s < 2):
                 break
+            if s > 1 and not cluster_fits(bn, s, paired):
+                continue
             ctas = tiles * s
             k_it = -(-num_k // s)
             cta_bytes = k_it * 64 * 2 * (bn + 0.35 * 128)
@@ -81,6 +100,25 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
             if best is None or t < best[0]:
                 best = (t, bn, s)
     return best[1], best[2]
+
+
+# Resident CTAs of the decode attention kernel on a B200 (148 SMs x 3).
+ATTN_SLOTS = 148 * 3
+ATTN_MAX_SPLIT = 8192
+
+
+def decode_split_tokens(n_seqs: int, n_kv: int, ctx_total: int, max_ctx: int,
+                        slots: int = ATTN_SLOTS) -> int:
+    """Keys per split-KV piece of a decode attention launch.  With at least
+    two CTAs per resident slot from (sequence, kv head) pairs alone, every
+    pair runs as one CTA (dispatched longest first, no merge); otherwise the
+    keys are cut so that about 2 x slots CTAs run.  A multiple of 16 in
+    [256, 8192]."""
+    if n_seqs * n_kv >= 2 * slots:
+        split = max_ctx
+    else:
+        split = -(-ctx_total * n_kv // (2 * slots))
+    return min(ATTN_MAX_SPLIT, max(256, -(-split // 16) * 16))
 
 
 # ------------------------------------------------------------------ weights
@@ -186,7 +224,8 @@ class StepMeta:
     Fields: ids, positions, slots [T]; row_dst [T] (sequence index of each
     sequence's last token, else -1); for the decode subset (q_len*G <= 16)
     and the prefill subset: q_start, q_len, ctx_len [n], block tables
-    [n, bt_ld] (-1 padded); the prefill (sequence, 64-row tile) work list."""
+    [n, bt_ld] (-1 padded); the decode subset's order by descending context
+    length; the prefill (sequence, 64-row tile) work list."""
 
     def __init__(self, token_ids, positions, seq_slices, block_tables, context_lens,
                  block_size: int, group: int, device, pinned: bool = True,
@@ -237,8 +276,10 @@ class StepMeta:
         p_idx, p_qs, p_ql, p_ctx, p_bt = subset(~is_dec)
         work = [(r, t) for r, ql in enumerate(p_ql) for t in range(-(-int(ql) * group // 64))]
         work = np.asarray(work, dtype=np.int32).reshape(-1, 2)
-        parts = [ids, pos, slots, row_dst, d_qs, d_ql, d_ctx, d_bt.ravel(), p_qs, p_ql, p_ctx,
-                 p_bt.ravel(), work.ravel()]
+        # decode sequences longest first: the attention grid dispatches in this order
+        d_order = np.argsort(-d_ctx, kind="stable").astype(np.int32)
+        parts = [ids, pos, slots, row_dst, d_qs, d_ql, d_ctx, d_bt.ravel(), d_order, p_qs, p_ql,
+                 p_ctx, p_bt.ravel(), work.ravel()]
         flat = np.concatenate(parts).astype(np.int32)
         host = torch.from_numpy(flat)
         if pinned and torch.device(device).type == "cuda":
@@ -259,7 +300,8 @@ class StepMeta:
             views.append(buf[o:o + a.size])
             o += a.size
         (self.ids, self.positions, self.slots, self.row_dst, self.dec_q_start, self.dec_q_len,
-         self.dec_ctx, dbt, self.pre_q_start, self.pre_q_len, self.pre_ctx, pbt, wk) = views
+         self.dec_ctx, dbt, self.dec_order, self.pre_q_start, self.pre_q_len, self.pre_ctx, pbt,
+         wk) = views
         self.dec_bt = dbt.view(len(d_idx), d_bt.shape[1])
         self.pre_bt = pbt.view(len(p_idx), p_bt.shape[1])
         self.work = wk.view(-1, 2)
@@ -281,12 +323,17 @@ class DeviceModel:
     """Buffers and the launch sequence of the forward on one rank."""
 
     def __init__(self, weights: RankWeights, max_tokens: int = 2048, max_seqs: int = 256,
-                 comm=None, split_tokens: int = 512):
+                 comm=None, split_tokens: int | None = None, l2_prefetch_bytes: int = 0):
         self.w = weights
         self.cfg = weights.cfg
         self.device = weights.device
         self.comm = comm
+        # decode split-KV size (None: decode_split_tokens per call)
         self.split_tokens = split_tokens
+        # bytes of the next projection's weight warmed into L2 during a GEMM
+        # epilogue (0: off; on the 14B decode step it lengthened the issuing
+        # GEMM by more than it saved the next one)
+        self.l2_prefetch_bytes = l2_prefetch_bytes
         # split-K scratch (arrival counters must stay zero between calls) and
         # split-KV attention scratch live in separate arenas
         self.scratch = ops.Scratch(self.device, 1 << 20)
@@ -321,7 +368,8 @@ class DeviceModel:
                                   self.hg_last, self.sq_last, self.logits, self.next_ids))
         d = cfg.d_model
         self.T_max, self.S_max = T, S
-        self.parts_max = max(-(-d // 64), 1)
+        # deferred-norm partial sums: one row per (column tile, cluster member)
+        self.parts_max = max(-(-d // 64), 1) * 8
         self.h = torch.zeros(T, d, device=dev)
         self.hg = torch.zeros(T, d, device=dev, dtype=torch.bfloat16)
         self.sq = torch.zeros(self.parts_max, T, device=dev)
@@ -340,33 +388,61 @@ class DeviceModel:
             self._alloc(max(T, self.T_max), max(S, self.S_max))
 
     # one row-parallel projection: residual (+ all-reduce) + norm prologue
-    def _row(self, x, wmat, g_next, T, last: bool, md: StepMeta, site: int):
-        bn, splits = plan_gemm(T, wmat.shape[0], wmat.shape[1])
-        kw = dict(bn=bn, splits=splits, scratch=self.scratch)
+    def _row(self, x, wmat, g_next, T, last: bool, md: StepMeta, site: int, plan, nxt):
+        bn, splits = plan
+        kw = dict(bn=bn, splits=splits, scratch=self.scratch, next_weight=nxt)
         if last:
             kw.update(row_dst=md.row_dst, hg2=self.hg_last, sq2=self.sq_last)
         Nn, K = wmat.shape
         nbytes = 2 * Nn * K + 2 * T * K + T * Nn * (4 + 4 + 2)
+        proj = "o_proj" if site % 2 == 0 else "down_proj"
         if self.comm is None:
-            self._run("row_gemm_residual", nbytes, 2.0 * T * Nn * K, ops.row_linear_residual, x,
+            self._run(f"{proj}_residual", nbytes, 2.0 * T * Nn * K, ops.row_linear_residual, x,
                       wmat, self.h[:T], g_next, self.hg[:T], self.sq, **kw)
         else:
-            self._run("row_gemm_allreduce_residual", nbytes, 2.0 * T * Nn * K,
+            self._run(f"{proj}_allreduce_residual", nbytes, 2.0 * T * Nn * K,
                       self.comm.row_linear_residual, x, wmat, self.h[:T], g_next, self.hg[:T],
                       self.sq, site=site, n_sites=2 * self.cfg.n_layers, **kw)
-        return -(-Nn // bn)
+        return ops.row_parts(Nn, bn, splits)
+
+    def plans(self, T: int, n: int) -> dict:
+        """(bn, splits) of every projection of a forward over T tokens with n
+        sampled rows (all layers share their shapes)."""
+        cfg, W = self.cfg, self.w
+        L = W.layers[0]
+        hd = cfg.head_dim
+        return {
+            "qkv": plan_gemm(T, L.wqkv.shape[0], cfg.d_model,
+                             bns=tuple(b for b in (64, 128, 192, 256) if b % hd == 0),
+                             paired=hd >= 32),
+            "o": plan_gemm(T, L.wo.shape[0], L.wo.shape[1]),
+            "gu": (RankWeights.GU_BN,
+                   plan_gemm(T, L.wgu.shape[0], cfg.d_model, bns=(RankWeights.GU_BN,),
+                             paired=True)[1]),
+            "down": plan_gemm(T, L.wd.shape[0], L.wd.shape[1]),
+            "lm": plan_gemm(n, cfg.vocab_size, cfg.d_model),
+        }
+
+    def _next(self, w: torch.Tensor, plan) -> "N.L2Prefetch | None":
+        return N.l2_next(w, plan[1], self.l2_prefetch_bytes)
 
     def forward(self, md: StepMeta, kv_pools: list[torch.Tensor], compute_logits: bool = True,
                 sample: bool = False, attn_max_ctx: int | None = None):
         """Launch the forward.  ``attn_max_ctx`` sizes the decode attention
         grid (default: this batch's longest context); a CUDA graph passes its
-        bound so one capture serves every context length up to it."""
+        bound so one capture serves every context length up to it.
+
+        Every GEMM whose epilogue is followed by another weight-streaming GEMM
+        asks for the next weight to be warmed into L2 (o_proj -> gate/up ->
+        down -> next layer's QKV or the LM head); the QKV projection is
+        followed by attention, whose KV stream would evict such lines."""
         cfg, W = self.cfg, self.w
         T, n = md.T, md.n_out
         self.ensure(T, n)
         d, hd = cfg.d_model, cfg.head_dim
         inv_d, eps = 1.0 / d, cfg.rms_eps
         bs = kv_pools[0].shape[3]
+        pl = self.plans(T, n)
         if self.comm is not None:
             self.comm.begin_step()
         self._run("embed", T * d * (2 + 4 + 2), 0.0, ops.embed, md.ids, W.emb, W.layers[0].ln_in,
@@ -377,8 +453,7 @@ class DeviceModel:
         parts = 1
         for li, L in enumerate(W.layers):
             pool = kv_pools[li]
-            bns = tuple(b for b in (64, 128, 192, 256) if b % hd == 0)
-            bn, splits = plan_gemm(T, L.wqkv.shape[0], d, bns=bns)
+            bn, splits = pl["qkv"]
             Nq = L.wqkv.shape[0]
             self._run("qkv_rope_kv", 2 * Nq * d + 2 * T * d + 2 * T * Nq, 2.0 * T * Nq * d,
                       ops.qkv_rope_kv, self.hg[:T], L.wqkv, L.bqkv, n_q_heads=W.n_q, n_kv_heads=W.n_kv,
@@ -389,33 +464,40 @@ class DeviceModel:
             akw = dict(n_q_heads=W.n_q, n_kv_heads=W.n_kv, head_dim=hd, block_size=bs)
             qrow = W.n_q * hd * 2
             if md.n_dec:
+                mc = attn_max_ctx or md.dec_max_ctx
+                split = self.split_tokens or decode_split_tokens(
+                    md.n_dec, W.n_kv, md.n_dec * mc if attn_max_ctx else md.dec_ctx_sum, mc)
                 self._run(
                     "attention_decode", dec_ctx * kv_row + 2 * md.dec_tokens * qrow,
                     4.0 * md.dec_ctx_sum * W.n_q * hd, ops.paged_attention_decode,
                     self.q, self.attn, pool, block_tables=md.dec_bt, q_start=md.dec_q_start,
-                    q_len=md.dec_q_len, ctx_len=md.dec_ctx,
-                    max_ctx=attn_max_ctx or md.dec_max_ctx,
-                    split_tokens=self.split_tokens, scratch=self.attn_scratch, **akw)
+                    q_len=md.dec_q_len, ctx_len=md.dec_ctx, seq_order=md.dec_order,
+                    max_ctx=mc, split_tokens=split, scratch=self.attn_scratch, **akw)
             if md.n_pre:
                 self._run(
                     "attention_prefill", pre_ctx * kv_row + 2 * (T - md.dec_tokens) * qrow,
                     4.0 * md.pre_pairs * W.n_q * hd, ops.paged_attention_prefill,
                     self.q, self.attn, pool, block_tables=md.pre_bt, q_start=md.pre_q_start,
                     q_len=md.pre_q_len, ctx_len=md.pre_ctx, work=md.work, **akw)
-            parts = self._row(self.attn[:T], L.wo, L.ln_post, T, False, md, 2 * li)
-            bn = RankWeights.GU_BN
-            _, splits = plan_gemm(T, L.wgu.shape[0], d, bns=(bn,))
+            parts = self._row(self.attn[:T], L.wo, L.ln_post, T, False, md, 2 * li, pl["o"],
+                              self._next(L.wgu, pl["gu"]))
+            bn, splits = pl["gu"]
             Ngu = L.wgu.shape[0]
             self._run("gate_up_swiglu", 2 * Ngu * d + 2 * T * d + 2 * T * W.ff, 2.0 * T * Ngu * d,
                       ops.gate_up_swiglu, self.hg[:T], L.wgu, self.act[:T], n_feat=W.ff,
                       sq=self.sq[:parts], inv_d=inv_d, eps=eps, bn=bn, splits=splits,
-                      scratch=self.scratch)
+                      scratch=self.scratch, next_weight=self._next(L.wd, pl["down"]))
             last = li == len(W.layers) - 1
             g_next = W.final_norm if last else W.layers[li + 1].ln_in
-            parts = self._row(self.act[:T, :W.ff], L.wd, g_next, T, last, md, 2 * li + 1)
+            if not last:
+                nxt = self._next(W.layers[li + 1].wqkv, pl["qkv"])
+            else:
+                nxt = self._next(W.lm_head, pl["lm"]) if compute_logits else None
+            parts = self._row(self.act[:T, :W.ff], L.wd, g_next, T, last, md, 2 * li + 1,
+                              pl["down"], nxt)
         if not compute_logits:
             return None
-        bn, splits = plan_gemm(n, cfg.vocab_size, d)
+        bn, splits = pl["lm"]
         out = self.logits[:n]
         V = cfg.vocab_size
         self._run("lm_head", 2 * V * d + 2 * n * d + 4 * n * V, 2.0 * n * V * d, ops.linear,
