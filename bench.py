@@ -351,11 +351,16 @@ def run_ours(args) -> None:
     per_launch_bytes = tk["bytes"] / tk["launches"]
     per_launch_s = tk["ms"] / tk["launches"] / 1e3
     achieved = per_launch_bytes / per_launch_s / 1e9
+    # DRAM bytes per launch of the top kernel: the ratio of ncu-measured
+    # traffic to algorithmic bytes in a captured small case of the same
+    # kernel (profiles/traffic.json), scaled to this launch's algorithmic bytes
     traffic = None
     tr_path = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tr_path):
         with open(tr_path) as f:
-            traffic = json.load(f).get(f"{top}@tp{world}")
+            rec = json.load(f).get(f"{top}@tp{world}")
+        if rec:
+            traffic = per_launch_bytes * rec["dram_bytes_per_launch"] / rec["algorithmic_bytes_per_launch"]
 
     line = None
     if rank == 0:

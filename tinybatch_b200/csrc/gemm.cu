@@ -376,9 +376,11 @@ __device__ __forceinline__ void pack_bf16x16(const float* v, uint4& lo, uint4& h
   hi.w = pack_bf16x2(v[14], v[15]);
 }
 
-// One system fence (cumulative: it orders the CTA's pushes, which the caller
-// made visible to this thread with a CTA barrier after each thread's own
-// fence), then a relaxed flag store to every rank.
+// One system fence by one thread, then a relaxed flag store to every rank.
+// The caller's CTA barrier puts every epilogue thread's pushes before this
+// thread's fence in causality order, and a release fence is cumulative, so
+// the flag publishes the whole CTA's pushes (no fence per thread: each would
+// wait for its own NVLink writes to be acknowledged).
 template <class F>
 __device__ __forceinline__ void signal_peers(const CommDev& c, F flag_of, uint32_t epoch) {
   fence_sys();
@@ -445,7 +447,6 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
       for (int p = 0; p < c.world; ++p) put16(rs_at(p, c.rank), u, v);
     }
   }
-  fence_sys();
   epi_bar();
   if (leader) {
     trace_at(g, TR_PUSHED);
@@ -508,7 +509,6 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
     sum_partials(u, v);
     for (int p = 0; p < c.world; ++p) put16(c.ag[p] + ag_off, u, v);
   }
-  fence_sys();
   epi_bar();
   if (leader) {
     signal_peers(c, [&](int p) { return flag_at(p, 1, c.rank); }, epoch);
