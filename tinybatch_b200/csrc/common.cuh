@@ -119,39 +119,34 @@ __device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* smem_raw) {
 
 // ------------------------------------------------------ cross-GPU signalling
 
-__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
 }
 
 // Peer waits get a longer budget than pipeline waits: ranks may drift apart
 // by host-side work between steps.
 constexpr uint64_t PEER_BUDGET_NS = 5000000000ull;
 
-// Bounded wait until *p == v, written by another GPU after a system fence.
-// Polls with relaxed loads; the fence after the match gives the acquire.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *p == v, written by another GPU with a release store.
+// Polls with acquire loads (measured on B200 over NVLink: a release store
+// and acquire polling cost about what relaxed accesses do, while a system
+// fence adds ~1.5 us per side, more when many CTAs fence at once).
 __device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t v) {
-  if (ld_relaxed_sys(p) != v) {
+  if (ld_acquire_sys(p) != v) {
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1; ld_relaxed_sys(p) != v; ++i) {
+    for (uint32_t i = 1; ld_acquire_sys(p) != v; ++i) {
       if ((i & 1023u) == 0 && globaltimer_ns() - t0 > PEER_BUDGET_NS) {
         set_status(ERR_PEER_TIMEOUT);
         return false;
       }
     }
   }
-  fence_sys();
   return true;
 }
 

@@ -376,15 +376,14 @@ __device__ __forceinline__ void pack_bf16x16(const float* v, uint4& lo, uint4& h
   hi.w = pack_bf16x2(v[14], v[15]);
 }
 
-// One system fence by one thread, then a relaxed flag store to every rank.
-// The caller's CTA barrier puts every epilogue thread's pushes before this
-// thread's fence in causality order, and a release fence is cumulative, so
-// the flag publishes the whole CTA's pushes (no fence per thread: each would
-// wait for its own NVLink writes to be acknowledged).
+// A release store of the flag to every rank, by one thread.  The caller's
+// CTA barrier puts every epilogue thread's pushes before this thread's
+// release in causality order, and release is cumulative, so the flag
+// publishes the whole CTA's pushes (no fence per thread: each would wait
+// for its own NVLink writes to be acknowledged).
 template <class F>
 __device__ __forceinline__ void signal_peers(const CommDev& c, F flag_of, uint32_t epoch) {
-  fence_sys();
-  for (int p = 0; p < c.world; ++p) st_relaxed_sys(flag_of(p), epoch);
+  for (int p = 0; p < c.world; ++p) st_release_sys(flag_of(p), epoch);
 }
 
 // Row-parallel epilogue with the all-reduce across tensor-parallel ranks

@@ -67,12 +67,14 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
               paired: bool = False) -> tuple[int, int]:
     """Tile width and cluster split-K factor for C[M,N] = A[M,K] B[N,K]^T.
 
-    Time model (fitted to B200 measurements of the decode shapes): a CTA
-    streams its B slice plus ~35% of its A slice (the rest hits L2) at
-    min(50 GB/s, 6 TB/s / active CTAs) or is bound by its share of the
-    tensor pipe (~10.8 TFLOP/s per SM); ~1 us of epilogue and 0.25 us per
-    extra cluster member for the DSMEM reduction.  A launch with more CTAs
-    than fit at once runs (CTAs / resident CTAs) waves of fully busy SMs.
+    Time model, fitted to device timelines of the decode shapes on B200:
+    a CTA streams its B slice plus ~35% of its A slice (the rest hits L2) at
+    min(50 GB/s, 6 TB/s / active CTAs), or is bound by its share of the
+    tensor pipe (~10.8 TFLOP/s per SM); its epilogue then costs ~1.5 us of
+    launch and prologue, ~0.9 us per 16-column chunk it finishes and, with
+    split-K, one cluster barrier (~1.3 us) plus the partial chunks it stores
+    into the other members' shared memory at ~25 GB/s.  A launch with more
+    CTAs than fit at once runs (CTAs / resident CTAs) waves.
     ``paired``: the epilogue finishes chunk pairs (SwiGLU, RoPE); only
     (bn, splits) whose cluster chunks fit shared memory are considered."""
     cap = _cluster_capacity()
@@ -90,13 +92,15 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
             k_it = -(-num_k // s)
             cta_bytes = k_it * 64 * 2 * (bn + 0.35 * 128)
             cta_flops = 2.0 * 128 * bn * 64 * k_it
-            fixed = 1e-6 + 0.25e-6 * (s - 1)
+            epi = 1.5e-6 + 0.9e-6 * (bn / 16) / s
+            if s > 1:
+                epi += 1.3e-6 + (bn * 128 * 4 * (s - 1) / s) / 25e9
             if tiles <= cap[s - 1]:
                 bw = min(50e9, 6.0e12 / ctas)
-                t = max(cta_bytes / bw, cta_flops / 10.8e12) + fixed
+                t = max(cta_bytes / bw, cta_flops / 10.8e12) + epi
             else:     # several waves of fully busy SMs (39 GB/s each)
                 waves = ctas / (cap[s - 1] * s)
-                t = waves * (max(cta_bytes / 39e9, cta_flops / 10.8e12) + fixed)
+                t = waves * (max(cta_bytes / 39e9, cta_flops / 10.8e12) + epi)
             if best is None or t < best[0]:
                 best = (t, bn, s)
     return best[1], best[2]
