@@ -51,6 +51,9 @@ GEMM_CASES = [
     (128, 960, 2048, 192, 4),
     (100, 384, 4096, 64, 8),
     (128, 1280, 2048, 256, 6),
+    # more tiles than SMs: persistent CTAs walk several tiles each
+    (1024, 4608, 512, 128, 1),
+    (777, 5120, 320, 256, 1),
 ]
 
 
@@ -86,7 +89,8 @@ def test_linear_rowscale_bf16():
     (128, 512, 640, 128, 1, "cluster"), (37, 256, 1024, 64, 4, "global"),
     (37, 256, 1024, 64, 4, "cluster"), (260, 896, 896, 128, 1, "cluster"),
     (128, 5120, 5120, 256, 7, "cluster"), (96, 896, 896, 192, 3, "cluster"),
-    (128, 2048, 2048, 256, 8, "cluster"), (20, 640, 1280, 128, 5, "cluster")])
+    (128, 2048, 2048, 256, 8, "cluster"), (20, 640, 1280, 128, 5, "cluster"),
+    (1100, 5120, 256, 128, 1, "cluster"), (1024, 2048, 192, 64, 1, "cluster")])
 def test_row_linear_residual(M, N, K, bn, splits, mode):
     x = _rand(M, K, seed=5)
     w = _rand(N, K, scale=1 / math.sqrt(K), seed=6)
@@ -117,7 +121,8 @@ def test_row_linear_residual(M, N, K, bn, splits, mode):
     (128, 256, 512, 128, 1, "cluster"), (50, 192, 896, 128, 2, "global"),
     (50, 192, 896, 128, 2, "cluster"), (200, 128, 256, 256, 1, "cluster"),
     (128, 1728, 640, 192, 2, "cluster"), (128, 864, 1024, 192, 1, "cluster"),
-    (128, 992, 1024, 256, 3, "cluster"), (64, 720, 1280, 192, 5, "cluster")])
+    (128, 992, 1024, 256, 3, "cluster"), (64, 720, 1280, 192, 5, "cluster"),
+    (700, 3456, 256, 192, 1, "cluster")])
 def test_gate_up_swiglu(M, F, K, bn, splits, mode):
     x = _rand(M, K, seed=8)
     wg = _rand(F, K, scale=1 / math.sqrt(K), seed=9)
@@ -145,9 +150,10 @@ def test_gate_up_swiglu(M, F, K, bn, splits, mode):
     (4, 2, 16, 64, 16, 1), (14, 2, 64, 128, 16, 1), (40, 8, 128, 128, 16, 1),
     (5, 1, 128, 256, 4, 1), (40, 8, 128, 256, 16, 4), (14, 2, 64, 192, 16, 2),
     (5, 1, 128, 128, 16, 3), (4, 2, 16, 64, 16, 2), (14, 2, 64, 256, 16, 3),
-    (40, 8, 128, 256, 16, 5)])
+    (40, 8, 128, 256, 16, 5), (40, 8, 128, 128, 16, 1), (14, 2, 64, 64, 16, 1)])
 def test_qkv_rope_kv(hq, hkv, hd, bn, bs, splits):
-    M, K = 70, max(256, 128 * splits)
+    # 1000 rows with one split: more tiles than SMs (persistent CTAs)
+    M, K = (1000 if splits == 1 and bn <= 128 else 70), max(256, 128 * splits)
     N = (hq + 2 * hkv) * hd
     x = _rand(M, K, seed=11)
     w = _rand(N, K, scale=1 / math.sqrt(K), seed=12)

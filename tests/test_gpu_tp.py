@@ -99,7 +99,8 @@ def _op_worker(rank, world, port, cases, queue):
 @pytest.mark.parametrize("two_shot", [False, True])
 def test_fused_row_gemm_allreduce_world2(two_shot):
     cases = [(1, 5120, 5120, 256, 4, two_shot), (64, 5120, 1024, 128, 2, two_shot),
-             (300, 896, 896, 128, 1, two_shot), (128, 5120, 13824, 192, 4, two_shot)]
+             (300, 896, 896, 128, 1, two_shot), (128, 5120, 13824, 192, 4, two_shot),
+             (2048, 5120, 512, 128, 1, two_shot)]   # 640 tiles: several per persistent CTA
     res = _spawn(2, _op_worker, (cases,), port=PORT + 7, timeout_s=240, collect_all=True)
     r0, r1 = res[0], res[1]
     for (err, sq_err, code, hsum0), (_, _, code1, hsum1) in zip(r0, r1):

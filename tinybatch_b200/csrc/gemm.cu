@@ -405,7 +405,8 @@ __device__ __forceinline__ void signal_peers(const CommDev& c, F flag_of, uint32
 template <int BN>
 __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader<BN>& acc, int tm,
                                            int tn, int row, int own, int n_own,
-                                           const ResidPre& pre) {
+                                           const ResidPre& pre, int flag_slot,
+                                           uint64_t* acc_free) {
   const CommDev& c = g.comm;
   const int m = tm * BM + row;
   const bool valid = m < g.M;
@@ -414,7 +415,7 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
   const int par = (int)(epoch & 1u);
   // plane: every tile of a max_rows x n_cols output, padded to whole tiles
   const size_t plane = (size_t)((c.max_rows + BM - 1) / BM) * BM * (size_t)(c.n_cols + 256);
-  const int cta = blockIdx.x;
+  const int cta = flag_slot;   // this CTA's (tile's) flags: same index on every rank
   const int per_owner = N / c.world;
   const bool leader = threadIdx.x == 64;
   constexpr int U = BN / 16;
@@ -446,7 +447,10 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
       for (int p = 0; p < c.world; ++p) put16(rs_at(p, c.rank), u, v);
     }
   }
+  // the accumulator has been read: a persistent CTA's MMA warp may reuse it
+  if (acc_free != nullptr) tc_fence_before();
   epi_bar();
+  if (acc_free != nullptr && leader) mbar_arrive(acc_free);
   if (leader) {
     trace_at(g, TR_PUSHED);
     signal_peers(c, [&](int p) { return flag_at(p, 0, c.rank); }, epoch);
@@ -669,24 +673,28 @@ __device__ __forceinline__ void fin_prefetch(const GemmArgs& g, int tm, int tn, 
     load_fin_inputs(g, tm, fin_row(t), tn * BN + own * 16 + 4 * fin_piece(t), p);
 }
 
-// h += acc; hg = bf16(h * g_next) (and its copy in row dst of hg2); the
-// CTA's partial sums of h^2 per row -> row `part` of sq_out / sq2.  One
-// rolled loop over the chunks (the epilogue runs once per CTA, from a cold
-// instruction cache: compact code matters), each chunk's inputs loaded one
-// chunk ahead.
+// h += acc; hg = bf16(h * g_next) (and its copy in row dst of hg2), for the
+// chunks p0, p0 + step, ... below p_end (staging slots 0, 1, ...); the row
+// sums of the new h^2 are added to ss (this thread's 4 rows).  One rolled
+// loop over the chunks (the epilogue code runs from a cold instruction cache:
+// compact code matters), each chunk's inputs loaded one chunk ahead; the first
+// chunk's come from `pre` when given.
 template <int BN>
 __device__ __forceinline__ void finish_resid(const GemmArgs& g, const RowStage& rw,
                                              const uint8_t* smem, int nsrc, int nslot, int tm,
-                                             int tn, int own, int n_own, int part, int t,
-                                             const FinPre& pre) {
-  constexpr int U = BN / 16;
+                                             int tn, int p0, int p_end, int step, int t,
+                                             const FinPre* pre, float* ss) {
+  const int U = min(BN / 16, p_end);
   const int i = fin_piece(t), r0 = fin_row(t);
-  float ss[4] = {0.f, 0.f, 0.f, 0.f};
-  FinPre cur = pre;
+  FinPre cur;
+  if (p0 < U && tn * BN + p0 * 16 < g.N) {
+    if (pre != nullptr) cur = *pre;
+    else load_fin_inputs(g, tm, r0, tn * BN + p0 * 16 + 4 * i, cur);
+  }
   int lp = 0;
 #pragma unroll 1
-  for (int u = own; u < U && tn * BN + u * 16 < g.N; u += n_own, ++lp) {
-    const int un = u + n_own;
+  for (int u = p0; u < U && tn * BN + u * 16 < g.N; u += step, ++lp) {
+    const int un = u + step;
     FinPre nxt;
     if (un < U && tn * BN + un * 16 < g.N)
       load_fin_inputs(g, tm, r0, tn * BN + un * 16 + 4 * i, nxt);
@@ -710,18 +718,22 @@ __device__ __forceinline__ void finish_resid(const GemmArgs& g, const RowStage& 
       const int dst = rw.dst[row];
       if (dst >= 0) *reinterpret_cast<uint2*>(g.hg2 + (size_t)dst * g.ld_hg + n) = o;
     }
-    if (lp == 0 && threadIdx.x == 64) trace_at(g, TR_COMBINED);
     cur = nxt;
   }
-  if (threadIdx.x == 64) trace_at(g, TR_BODY);
+}
+
+// The row sums of h^2 a finisher thread accumulated (4 rows, its 4 columns
+// of each chunk), reduced over the 4 threads of each row -> row `part` of
+// sq_out / sq2.
+__device__ __forceinline__ void store_ss(const GemmArgs& g, int tm, int part, int t, float* ss) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], 8);
     ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], 16);
   }
-  if (i == 0) {
+  if (fin_piece(t) == 0) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) store_row_sumsq(g, tm, part, r0 + 32 * j, ss[j]);
+    for (int j = 0; j < 4; ++j) store_row_sumsq(g, tm, part, fin_row(t) + 32 * j, ss[j]);
   }
 }
 
@@ -729,9 +741,10 @@ __device__ __forceinline__ void finish_resid(const GemmArgs& g, const RowStage& 
 template <int BN, int EPI>
 __device__ __forceinline__ void finish_linear(const GemmArgs& g, const RowStage& rw,
                                               const uint8_t* smem, int nsrc, int nslot, int tm,
-                                              int tn, int own, int n_own, int t) {
+                                              int tn, int own, int p_end, int n_own, int t) {
   const int i = fin_piece(t), r0 = fin_row(t);
-  for (int u = own, lp = 0; u < BN / 16; u += n_own, ++lp) {
+  const int U = min(BN / 16, p_end);
+  for (int u = own, lp = 0; u < U; u += n_own, ++lp) {
     const int n = tn * BN + u * 16 + 4 * i;
     if (tn * BN + u * 16 >= g.N) break;
     float4 acc4[4];
@@ -764,9 +777,10 @@ __device__ __forceinline__ void finish_linear(const GemmArgs& g, const RowStage&
 template <int BN>
 __device__ __forceinline__ void finish_swiglu(const GemmArgs& g, const RowStage& rw,
                                               const uint8_t* smem, int nsrc, int nslot, int tm,
-                                              int tn, int own, int n_own, int t) {
+                                              int tn, int own, int p_end, int n_own, int t) {
   const int i = fin_piece(t), r0 = fin_row(t);
-  for (int p = own, lp = 0; p < BN / 32; p += n_own, ++lp) {
+  const int NP = min(BN / 32, p_end);
+  for (int p = own, lp = 0; p < NP; p += n_own, ++lp) {
     const int f0 = tn * (BN / 2) + p * 16;
     if (f0 >= g.n_feat) break;
     float4 ga4[4], ua4[4];
@@ -800,14 +814,15 @@ __device__ __forceinline__ void finish_swiglu(const GemmArgs& g, const RowStage&
 template <int BN>
 __device__ __forceinline__ void finish_qkv(const GemmArgs& g, const RowStage& rw, const uint8_t* smem,
                                            int nsrc, int nslot, int tm, int tn, int own,
-                                           int n_own, int t) {
+                                           int p_end, int n_own, int t) {
   const int i = fin_piece(t), r0 = fin_row(t);
   const int hd = g.head_dim, half = hd >> 1;
   const int heads_in_tile = BN / hd;
   const int total_heads = g.n_q_heads + 2 * g.n_kv_heads;
   const TileUnits tu = tile_units<BN, EPI_QKV>(g);
   const int per_head = tu.kind == 2 ? tu.hc : 1;
-  for (int p = own, lp = 0; p < tu.np; p += n_own, ++lp) {
+  const int NP = min(tu.np, p_end);
+  for (int p = own, lp = 0; p < NP; p += n_own, ++lp) {
     const int hh = p / per_head, jj = p % per_head;
     const int head = tn * heads_in_tile + hh;
     if (hh >= heads_in_tile || head >= total_heads) break;
@@ -894,18 +909,21 @@ __device__ __forceinline__ void finish_qkv(const GemmArgs& g, const RowStage& rw
   }
 }
 
+// Finish the pairs p0, p0 + step, ... below p_end of tile (tm, tn) from the
+// staging area (nsrc sources of nslot chunks; the k-th pair at slots
+// k * cp + which).  EPI_RESID adds its row sums of h^2 to ss.
 template <int BN, int EPI>
 __device__ __forceinline__ void finish(const GemmArgs& g, const RowStage& rw, const uint8_t* smem,
-                                       int nsrc, int nslot, int tm, int tn, int own, int n_own,
-                                       int part, int t, const FinPre& pre) {
+                                       int nsrc, int nslot, int tm, int tn, int p0, int p_end,
+                                       int step, int t, const FinPre* pre, float* ss) {
   if constexpr (EPI == EPI_RESID)
-    finish_resid<BN>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, part, t, pre);
+    finish_resid<BN>(g, rw, smem, nsrc, nslot, tm, tn, p0, p_end, step, t, pre, ss);
   else if constexpr (EPI == EPI_SWIGLU)
-    finish_swiglu<BN>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, t);
+    finish_swiglu<BN>(g, rw, smem, nsrc, nslot, tm, tn, p0, p_end, step, t);
   else if constexpr (EPI == EPI_QKV)
-    finish_qkv<BN>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, t);
+    finish_qkv<BN>(g, rw, smem, nsrc, nslot, tm, tn, p0, p_end, step, t);
   else
-    finish_linear<BN, EPI>(g, rw, smem, nsrc, nslot, tm, tn, own, n_own, t);
+    finish_linear<BN, EPI>(g, rw, smem, nsrc, nslot, tm, tn, p0, p_end, step, t);
 }
 
 template <int BN, int STAGES, int EPI>
@@ -1060,10 +1078,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (threadIdx.x == 64) trace_at(g, TR_CLUSTER_SYNC);
     if (warp >= 2) {
       if (tp) {
-        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, z, S, pre);
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, z, S, pre, blockIdx.x, nullptr);
         store_row_sumsq(g, tm, tn * S + z, row, ss);
       } else {
-        finish<BN, EPI>(g, rw, smem, S, nslot, tm, tn, z, S, tn * S + z, t, fpre);
+        float ss[4] = {0.f, 0.f, 0.f, 0.f};
+        finish<BN, EPI>(g, rw, smem, S, nslot, tm, tn, z, 1 << 30, S, t, &fpre, ss);
+        if constexpr (EPI == EPI_RESID) store_ss(g, tm, tn * S + z, t, ss);
       }
       if (threadIdx.x == 64) trace_at(g, TR_END);
     }
@@ -1097,13 +1117,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     if (run) {
       if (tp) {
-        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre);
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre, blockIdx.x, nullptr);
         store_row_sumsq(g, tm, tn, row, ss);
       } else {
         if (mode == SPLIT_GLOBAL) stage_global<BN>(acc, tu, smem, nslot, row);
         else stage_acc<BN>(acc, tu, 1, 0, smem, nslot, row, false);
         epi_bar();   // staged chunks and per-row values visible to every finisher thread
-        finish<BN, EPI>(g, rw, smem, 1, nslot, tm, tn, 0, 1, tn, t, fpre);
+        float ss[4] = {0.f, 0.f, 0.f, 0.f};
+        finish<BN, EPI>(g, rw, smem, 1, nslot, tm, tn, 0, 1 << 30, 1, t, &fpre, ss);
+        if constexpr (EPI == EPI_RESID) store_ss(g, tm, tn, t, ss);
       }
     }
     if (threadIdx.x == 64) trace_at(g, TR_END);
@@ -1113,6 +1135,208 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (mode == SPLIT_CLUSTER || mbar_wait(done, 0)) l2_prefetch_share(g.pf, &tma_pf, lane);
   }
 
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TCOLS);
+  }
+}
+
+// ------------------------------------------------------- persistent kernel
+// Launches without split-K run persistent: one CTA per SM walks the tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ...; the MMA warp alternates between
+// two TMEM accumulators, so tile i's epilogue (and, across tensor-parallel
+// ranks, its NVLink exchange) overlaps tile i+1's main loop.  The epilogue
+// stages 4 chunks at a time in a dedicated shared-memory area (the stage
+// ring keeps streaming the next tile) and finishes them with the finisher
+// layout.
+template <int BN, int STAGES>
+struct PersistLayout {
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = STAGES * A_BYTES;
+  static constexpr int OFF_STAGE = OFF_B + STAGES * B_BYTES;
+  static constexpr int STAGE_CHUNKS = 4;
+  static constexpr int OFF_BAR = OFF_STAGE + STAGE_CHUNKS * BM * 16 * 4;
+  static constexpr int BAR_BYTES = (2 * STAGES + 4) * 8 + 16 + 4 * BM * 4;
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
+  static_assert(SMEM <= 232448, "persistent GEMM shared memory above 227 KiB");
+};
+
+// Tile (tm, tn) of linear tile index `tile`: m fastest inside groups of
+// group_m row tiles (A tiles of a group stay in L2 while N advances).
+__device__ __forceinline__ void tile_coords(const GemmArgs& g, int tile, int& tm, int& tn) {
+  const int per_group = g.group_m * g.tiles_n;
+  const int first_m = (tile / per_group) * g.group_m;
+  const int gsize = min(g.tiles_m - first_m, g.group_m);
+  tm = first_m + (tile % per_group) % gsize;
+  tn = (tile % per_group) / gsize;
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tma_a,
+                           const __grid_constant__ CUtensorMap tma_b, const GemmArgs g) {
+  using L = PersistLayout<BN, STAGES>;
+  constexpr uint32_t TC = tmem_cols(BN);
+  constexpr uint32_t TCOLS = 2 * TC;
+  static_assert(TCOLS <= 512, "two accumulators must fit TMEM");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  uint8_t* sA = smem + L::OFF_A;
+  uint8_t* sB = smem + L::OFF_B;
+  uint8_t* stage = smem + L::OFF_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* row_rs = reinterpret_cast<float*>(tmem_slot + 4);
+  int* row_pos = reinterpret_cast<int*>(row_rs + BM);
+  int* row_slot = row_pos + BM;
+  int* row_dst = row_slot + BM;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = g.tiles_m * g.tiles_n;
+  const int num_k = (g.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 1);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TCOLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) {
+    pdl_trigger();
+    trace_at(g, TR_START);
+  }
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: one continuous ring over all tiles
+    pdl_wait();
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      int tm, tn;
+      tile_coords(g, tile, tm, tn);
+      for (int kb = 0; kb < num_k; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], A_BYTES + L::B_BYTES);
+        tma_load_2d(sA + s * A_BYTES, &tma_a, &full[s], kb * BK, tm * BM);
+        tma_load_2d(sB + s * L::B_BYTES, &tma_b, &full[s], kb * BK, tn * BN);
+      }
+    }
+    trace_at(g, TR_LOADS_ISSUED);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer: accumulator i & 1 for the CTA's i-th tile
+    constexpr uint32_t idesc = idesc_bf16_m128(BN);
+    int it = 0, i = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++i) {
+      const int b = i & 1, use = i >> 1;
+      if (use > 0 && !mbar_wait(&acc_empty[b], (use - 1) & 1)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + (uint32_t)(b * TC);
+      for (int kb = 0; kb < num_k; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&full[s], (it / STAGES) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * L::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          tc_mma_bf16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      if (ok) tc_commit(&acc_full[b]);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue: tile by tile, overlapping the next main loop
+    const int q = warp & 3;
+    const int row = q * 32 + lane;   // TMEM lane of this thread
+    const int t = threadIdx.x - 64;  // finisher thread index
+    const TileUnits tu = tile_units<BN, EPI>(g);
+    const int PG = L::STAGE_CHUNKS / tu.cp;   // pairs per staged group
+    const RowStage rw{row_rs, row_pos, row_slot, row_dst};
+    const bool tp = EPI == EPI_RESID && g.comm.world > 1;
+    AccReader<BN> acc;
+    acc.mode = SPLIT_NONE;
+    acc.splits = 1;
+    acc.z = 0;
+    acc.row = row;
+    acc.ws = nullptr;
+    acc.smem = stage;
+    acc.nslot = L::STAGE_CHUNKS;
+    pdl_wait();   // the epilogue reads and writes buffers earlier kernels use
+    int i = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+      int tm, tn;
+      tile_coords(g, tile, tm, tn);
+      const int b = i & 1, use = i >> 1;
+      epi_bar();   // the previous tile's finisher is done with the per-row arrays
+      stage_rows<EPI>(g, rw, tm, row);
+      ResidPre pre;
+      if constexpr (EPI == EPI_RESID) {
+        if (tp) resid_prefetch<BN>(g, tm, tn, row, 0, 1, pre);
+      }
+      if (!mbar_wait(&acc_full[b], use & 1)) break;
+      tc_fence_after();
+      acc.taddr = tmem_base + (uint32_t)(b * TC) + ((uint32_t)(q * 32) << 16);
+      if (tp) {
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre, tile, &acc_empty[b]);
+        store_row_sumsq(g, tm, tn, row, ss);
+        continue;
+      }
+      float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int p0 = 0; p0 < tu.np; p0 += PG) {
+        // stage the group's chunks from TMEM (one row per thread)
+        for (int k = 0; k < PG && p0 + k < tu.np; ++k) {
+          for (int which = 0; which < tu.cp; ++which) {
+            float v[16];
+            tmem_ld16(acc.taddr + 16 * tu.chunk(p0 + k, which), v);
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4)
+              *reinterpret_cast<float4*>(stage + stage_off(0, k * tu.cp + which, L::STAGE_CHUNKS,
+                                                           row, c4)) =
+                  make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+          }
+        }
+        const bool last = p0 + PG >= tu.np;
+        if (last) tc_fence_before();
+        epi_bar();   // staged chunks (and, first time, per-row values) visible to all
+        if (last && threadIdx.x == 64) mbar_arrive(&acc_empty[b]);   // accumulator reusable
+        finish<BN, EPI>(g, rw, stage, 1, L::STAGE_CHUNKS, tm, tn, p0, p0 + PG, 1, t, nullptr, ss);
+        epi_bar();   // the staging area is rewritten by the next group
+      }
+      if constexpr (EPI == EPI_RESID) store_ss(g, tm, tn, t, ss);
+    }
+    if (threadIdx.x == 64) trace_at(g, TR_END);
+  }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1147,9 +1371,48 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const CUtens
                     "gemm launch", ta, tb_, tpf, g);
 }
 
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <int BN, int STAGES, int EPI>
+static int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb_, const GemmArgs& g,
+                             cudaStream_t stream) {
+  using L = PersistLayout<BN, STAGES>;
+  auto kern = gemm_persistent_kernel<BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (e != cudaSuccess) return host_err(e, "persistent gemm smem attribute");
+    attr_set = true;
+  }
+  const int tiles = g.tiles_m * g.tiles_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  return launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), L::SMEM, stream, 1,
+                    "gemm persistent launch", ta, tb_, g);
+}
+
 template <int EPI>
 static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_,
                       const CUtensorMap& tpf, const GemmArgs& g, cudaStream_t stream) {
+  if (g.splits == 1 && g.ws == nullptr) {   // no split-K: persistent tiles
+    switch (bn) {
+      case 64: return launch_persistent<64, 7, EPI>(ta, tb_, g, stream);
+      case 128: return launch_persistent<128, 5, EPI>(ta, tb_, g, stream);
+      case 192: return launch_persistent<192, 4, EPI>(ta, tb_, g, stream);
+      case 256: return launch_persistent<256, 3, EPI>(ta, tb_, g, stream);
+      default: return arg_err("bn must be 64, 128, 192 or 256");
+    }
+  }
   switch (bn) {
     case 64: return launch_bn<64, 8, EPI>(ta, tb_, tpf, g, stream);
     case 128: return launch_bn<128, 6, EPI>(ta, tb_, tpf, g, stream);

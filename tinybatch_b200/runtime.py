@@ -74,7 +74,7 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
     launch and prologue, ~0.9 us per 16-column chunk it finishes and, with
     split-K, one cluster barrier (~1.3 us) plus the partial chunks it stores
     into the other members' shared memory at ~25 GB/s.  A launch with more
-    CTAs than fit at once runs (CTAs / resident CTAs) waves.
+    CTAs than fit at once runs ceil(CTAs / resident CTAs) waves.
     ``paired``: the epilogue finishes chunk pairs (SwiGLU, RoPE); only
     (bn, splits) whose cluster chunks fit shared memory are considered."""
     cap = _cluster_capacity()
@@ -98,8 +98,10 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
             if tiles <= cap[s - 1]:
                 bw = min(50e9, 6.0e12 / ctas)
                 t = max(cta_bytes / bw, cta_flops / 10.8e12) + epi
-            else:     # several waves of fully busy SMs (39 GB/s each)
-                waves = ctas / (cap[s - 1] * s)
+            else:     # several waves of fully busy SMs (39 GB/s each); a tail
+                # wave costs a whole wave (and, in a fused all-reduce, another
+                # exchange round trip)
+                waves = -(-ctas // (cap[s - 1] * s))
                 t = waves * (max(cta_bytes / 39e9, cta_flops / 10.8e12) + epi)
             if best is None or t < best[0]:
                 best = (t, bn, s)
