@@ -376,14 +376,23 @@ __device__ __forceinline__ void pack_bf16x16(const float* v, uint4& lo, uint4& h
   hi.w = pack_bf16x2(v[14], v[15]);
 }
 
-// A release store of the flag to every rank, by one thread.  The caller's
-// CTA barrier puts every epilogue thread's pushes before this thread's
-// release in causality order, and release is cumulative, so the flag
-// publishes the whole CTA's pushes (no fence per thread: each would wait
-// for its own NVLink writes to be acknowledged).
-template <class F>
-__device__ __forceinline__ void signal_peers(const CommDev& c, F flag_of, uint32_t epoch) {
-  for (int p = 0; p < c.world; ++p) st_release_sys(flag_of(p), epoch);
+// Flag handshake of one exchange round, run by the first epilogue warp: lane
+// p release-stores this CTA's flag into rank p, then lane s waits (acquire
+// loads, bounded) for rank s's flag.  The lanes work in parallel: a release
+// store waits for everything ordered before it, so one thread storing every
+// rank's flag in turn pays one NVLink round trip per rank.  The caller's CTA
+// barrier before puts every epilogue thread's pushes before each lane's
+// release (release is cumulative); its CTA barrier after makes the acquired
+// data visible to every thread.
+template <class FS, class FR>
+__device__ __forceinline__ void exchange_flags(const CommDev& c, FS send_flag, FR recv_flag,
+                                               uint32_t epoch) {
+  const int lane = threadIdx.x & 31;
+  if (lane < c.world) {
+    st_release_sys(send_flag(lane), epoch);
+    wait_flag_sys(recv_flag(lane), epoch);
+  }
+  __syncwarp();
 }
 
 // Row-parallel epilogue with the all-reduce across tensor-parallel ranks
@@ -418,6 +427,7 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
   const int cta = flag_slot;   // this CTA's (tile's) flags: same index on every rank
   const int per_owner = N / c.world;
   const bool leader = threadIdx.x == 64;
+  const bool flag_warp = (threadIdx.x >> 5) == 2;   // the first epilogue warp
   constexpr int U = BN / 16;
   const size_t tile_base = ((size_t)tm * g.tiles_n + tn) * U;
   auto xoff = [&](int u, int half) {
@@ -451,11 +461,11 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
   if (acc_free != nullptr) tc_fence_before();
   epi_bar();
   if (acc_free != nullptr && leader) mbar_arrive(acc_free);
-  if (leader) {
-    trace_at(g, TR_PUSHED);
-    signal_peers(c, [&](int p) { return flag_at(p, 0, c.rank); }, epoch);
-    for (int s = 0; s < c.world; ++s) wait_flag_sys(flag_at(c.rank, 0, s), epoch);
-    trace_at(g, TR_PARTNERS);
+  if (flag_warp) {
+    if (leader) trace_at(g, TR_PUSHED);
+    exchange_flags(c, [&](int p) { return flag_at(p, 0, c.rank); },
+                   [&](int s) { return flag_at(c.rank, 0, s); }, epoch);
+    if (leader) trace_at(g, TR_PARTNERS);
   }
   epi_bar();
 
@@ -513,10 +523,10 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
     for (int p = 0; p < c.world; ++p) put16(c.ag[p] + ag_off, u, v);
   }
   epi_bar();
-  if (leader) {
-    signal_peers(c, [&](int p) { return flag_at(p, 1, c.rank); }, epoch);
-    for (int s = 0; s < c.world; ++s) wait_flag_sys(flag_at(c.rank, 1, s), epoch);
-    trace_at(g, TR_SUMS);
+  if (flag_warp) {
+    exchange_flags(c, [&](int p) { return flag_at(p, 1, c.rank); },
+                   [&](int s) { return flag_at(c.rank, 1, s); }, epoch);
+    if (leader) trace_at(g, TR_SUMS);
   }
   epi_bar();
   // 3. every rank applies the same reduced sums
