@@ -8,7 +8,8 @@ W is stored transposed, [N, K/t], the F.linear layout the kernels read),
 summed over the t ranks, added to a residual and followed by the norm
 prologue -- one kernel per rank.  Each row reports the device time per call
 (CUDA graph of repeated calls, max over ranks), the same GEMM on one rank
-without the exchange, and the fraction of the roofline
+without the exchange, the all-reduce bus bandwidth over the fused call
+(`B_nvl / time`), and the fraction of the roofline
 
     T_roof = max(2 M (K/t) N / P_tensor,  B_hbm / BW_hbm,  B_nvl / BW_nvl)
     B_hbm  = 2 [(K/t) N + M (K/t) + 3 M N + N]      (bf16 bytes)
@@ -115,11 +116,15 @@ def run(ms: list[int], shapes=SHAPES, reps: int = 20, two_shot: bool | None = No
                 t_fused = _time_graph(fused, reps, world)
             t = t_fused if t_fused is not None else t_plain
             t_roof, bound = roofline_s(M, K, N, world, pk)
+            b_nvl = 2.0 * (world - 1) / world * 2 * M * N
             out.append({"M": M, "K": K, "N": N, "tp": world, "bn": bn, "splits": splits,
                         "us_fused": None if t_fused is None else round(t_fused * 1e6, 2),
                         "us_gemm_only": round(t_plain * 1e6, 2),
                         "us_roofline": round(t_roof * 1e6, 2), "bound": bound,
-                        "frac": round(t_roof / t, 4), "peaks": pk["source"]})
+                        "frac": round(t_roof / t, 4),
+                        # all-reduce bus bytes over the whole fused call (NCCL's busBw)
+                        "nvl_bus_GBps": round(b_nvl / t / 1e9, 1) if world > 1 else None,
+                        "peaks": pk["source"]})
         if comm is not None:
             comm.close()
     return out
