@@ -54,3 +54,83 @@ def test_step_meta_orders_decode_longest_first():
     assert np.all(np.diff(np.asarray(ctx)[order]) <= 0)
     assert order.tolist() == [1, 3, 2, 0, 4]      # stable among equal lengths
     assert md.dec_ctx.numpy().tolist() == ctx
+
+
+def _loop_pack(token_ids, positions, slices, tables, ctx, bs, group, bt_width):
+    """Plain-loop restatement of the StepMeta layout (the checker)."""
+    ids = np.asarray(token_ids, dtype=np.int32)
+    pos = np.asarray(positions, dtype=np.int32)
+    T, n = len(ids), len(slices)
+    starts = np.array([s for s, _ in slices], dtype=np.int32)
+    ends = np.array([e for _, e in slices], dtype=np.int32)
+    qlen = ends - starts
+    ctx = np.asarray(ctx, dtype=np.int32)
+    slots = np.full(T, -1, dtype=np.int32)
+    for i, (s, e) in enumerate(slices):
+        for t in range(s, e):
+            slots[t] = tables[i][pos[t] // bs] * bs + pos[t] % bs
+    row_dst = np.full(T, -1, dtype=np.int32)
+    for i, (s, e) in enumerate(slices):
+        if e > s:
+            row_dst[e - 1] = i
+    is_dec = qlen * group <= 16
+
+    def subset(mask):
+        idx = [i for i in range(n) if mask[i]]
+        ld = max([len(tables[i]) for i in idx] + [bt_width, 1])
+        bt = np.full((len(idx), ld), -1, dtype=np.int32)
+        for r, i in enumerate(idx):
+            bt[r, :len(tables[i])] = tables[i]
+        return starts[idx], qlen[idx], ctx[idx], bt, np.asarray(idx)
+
+    d = subset(is_dec)
+    p = subset(~is_dec)
+    order = np.argsort(-d[2], kind="stable").astype(np.int32)
+    work = [(r, t) for r, ql in enumerate(p[1]) for t in range(-(-int(ql) * group // 64))]
+    work = np.asarray(work, dtype=np.int32).reshape(-1, 2)
+    return np.concatenate([ids, pos, slots, row_dst, d[0], d[1], d[2], d[3].ravel(), order,
+                           p[0], p[1], p[2], p[3].ravel(), work.ravel()]).astype(np.int32)
+
+
+def test_step_meta_packing_matches_loop_restatement():
+    rng = np.random.default_rng(11)
+    for trial in range(30):
+        n = int(rng.integers(1, 40))
+        qlens = [int(rng.choice([1, 1, 1, int(rng.integers(2, 90))])) for _ in range(n)]
+        ctxs = [q + int(rng.integers(0, 300)) for q in qlens]
+        tables, nb = [], 0
+        for c in ctxs:
+            k = -(-c // 16) + int(rng.integers(0, 2))
+            tables.append(list(rng.permutation(5000)[:k]))
+        ids, pos, slices = [], [], []
+        for q, c in zip(qlens, ctxs):
+            s = len(ids)
+            ids += list(rng.integers(0, 1000, q))
+            pos += list(range(c - q, c))
+            slices.append((s, s + q))
+        bt_width = int(rng.choice([0, 40]))
+        md = StepMeta(ids, pos, slices, tables, ctxs, 16, 5, "cpu", pinned=False, bt_width=bt_width)
+        want = _loop_pack(ids, pos, slices, tables, ctxs, 16, 5, bt_width)
+        got = md.buf.numpy()
+        assert got.shape == want.shape and np.array_equal(got, want), trial
+
+
+def test_step_meta_rejects_position_beyond_table():
+    import pytest
+    with pytest.raises(IndexError):
+        StepMeta([1], [40], [(0, 1)], [[3, 4]], [41], 16, 4, "cpu", pinned=False)
+
+
+def test_token_view_matches_list():
+    from tinybatch_b200.scheduler import TokenView
+    p, o = list(range(100, 137)), list(range(900, 911))
+    full = p + o
+    for limit in (None, 0, 5, 37, 40, 48, 60):
+        v = TokenView(p, o, limit)
+        ref = full if limit is None else full[:limit]
+        assert len(v) == len(ref) and list(v) == ref
+        for a in range(-3, len(ref) + 3, 4):
+            for b in range(-3, len(ref) + 3, 5):
+                assert v[a:b] == ref[a:b], (limit, a, b)
+        for k in range(-len(ref), len(ref)):
+            assert v[k] == ref[k]

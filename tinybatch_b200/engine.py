@@ -25,6 +25,7 @@ from __future__ import annotations
 import time
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from .block_manager import BlockManager
@@ -114,6 +115,20 @@ class LLMEngine:
 
     # ------------------------------------------------------------ step
 
+    @staticmethod
+    def _table(req) -> np.ndarray:
+        """The request's block table as an int32 array, converted again only
+        when the list changed (decode steps append a block every block_size
+        tokens; preemption replaces the list)."""
+        t = req.block_table
+        cached = getattr(req, "_table_np", None)
+        # the cache holds the list itself: tables only grow in place or are
+        # replaced by a new list, so (same object, same length) means same content
+        if cached is None or cached[0] is not t or cached[1] != len(t):
+            cached = (t, len(t), np.asarray(t, dtype=np.int32))
+            req._table_np = cached
+        return cached[2]
+
     def build_batch(self, batch):
         bs = self.cfg.block_size
         ids: list[int] = []
@@ -131,12 +146,12 @@ class LLMEngine:
         for req in batch.decode:
             n = req.context_len()
             if len(req.block_table) * bs < n:
-                self.block_manager.append_slot(req.block_table, req.all_token_ids()[:-1])
+                self.block_manager.append_slot(req.block_table, req.token_view(n - 1))
             s = len(ids)
-            ids.append(req.all_token_ids()[-1])
+            ids.append(req.last_token_id())
             pos.append(n - 1)
             slices.append((s, s + 1))
-            tables.append(req.block_table)
+            tables.append(self._table(req))
             ctx.append(n)
         return ids, pos, slices, tables, ctx
 
@@ -154,7 +169,7 @@ class LLMEngine:
             g = self.decode_graph(len(ordered))
             md = StepMeta(ids, pos, slices, tables, ctx, self.cfg.block_size,
                           self.model.cfg.n_heads // self.model.cfg.n_kv_heads, self.device,
-                          bt_width=self._bt_width, dest=g.dest)
+                          bt_width=self._bt_width, dest=g.dest, staging=g.staging())
             g.run(md)
             logits = self.model.dm.logits[: len(ordered)]
         else:

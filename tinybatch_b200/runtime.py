@@ -19,6 +19,7 @@ per-tile partial sums of ``h^2``; the next GEMM multiplies its rows by
 """
 from __future__ import annotations
 
+import itertools
 import math
 from dataclasses import dataclass
 
@@ -225,7 +226,8 @@ def rope_tables(cfg: ModelConfig, device) -> tuple[torch.Tensor, torch.Tensor]:
 
 class StepMeta:
     """Device int32 metadata of one flat mixed batch, built on the host with
-    numpy and shipped in one host->device copy.
+    numpy and shipped in one host->device copy.  Block tables may be lists
+    or int numpy arrays.
 
     Fields: ids, positions, slots [T]; row_dst [T] (sequence index of each
     sequence's last token, else -1); for the decode subset (q_len*G <= 16)
@@ -236,11 +238,13 @@ class StepMeta:
     def __init__(self, token_ids, positions, seq_slices, block_tables, context_lens,
                  block_size: int, group: int, device, pinned: bool = True,
                  all_logits: bool = False, bt_width: int = 0,
-                 dest: torch.Tensor | None = None):
+                 dest: torch.Tensor | None = None, staging: torch.Tensor | None = None):
         """``bt_width`` pads the block tables to at least that many columns
         (a fixed layout for CUDA-graph replay); ``dest``, a device int32
         buffer of exactly the packed size, receives the metadata instead of
-        a fresh allocation."""
+        a fresh allocation; ``staging``, a pinned int32 host buffer at least
+        that large, is reused for the copy instead of pinning a new one (the
+        caller keeps it untouched until the copy has completed)."""
         if isinstance(token_ids, torch.Tensor):
             token_ids = token_ids.detach().cpu().numpy()
         if isinstance(positions, torch.Tensor):
@@ -253,13 +257,27 @@ class StepMeta:
         ends = np.fromiter((e for _, e in seq_slices), dtype=np.int32, count=n)
         qlen = ends - starts
         ctx = np.asarray(context_lens, dtype=np.int32)
+        # block tables as one flat array with row offsets (one pass over the lists)
+        lens = np.fromiter(map(len, block_tables), dtype=np.int64, count=n)
+        offs = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(lens, out=offs[1:])
+        if n and all(isinstance(t, np.ndarray) for t in block_tables):
+            flat_bt = np.concatenate(block_tables).astype(np.int64, copy=False)
+        else:
+            flat_bt = np.fromiter(itertools.chain.from_iterable(block_tables), dtype=np.int64,
+                                  count=int(offs[-1]))
         # slot of every token: table[p // bs] * bs + p % bs
-        slots = np.empty(T, dtype=np.int32)
-        for i, ((s, e), table) in enumerate(zip(seq_slices, block_tables)):
-            if e > s:
-                tbl = np.asarray(table, dtype=np.int64)
-                p = pos[s:e].astype(np.int64)
-                slots[s:e] = (tbl[p // block_size] * block_size + p % block_size).astype(np.int32)
+        slots = np.full(T, -1, dtype=np.int32)
+        n_tok = int(qlen.sum())
+        if n_tok:
+            tok_seq = np.repeat(np.arange(n), qlen)
+            first_of_seq = np.repeat(np.cumsum(qlen) - qlen, qlen)
+            tok = np.arange(n_tok) - first_of_seq + np.repeat(starts, qlen)
+            p = pos[tok].astype(np.int64)
+            blk = p // block_size
+            if np.any(blk >= lens[tok_seq]) or np.any(p < 0):
+                raise IndexError("a token position lies beyond its sequence's block table")
+            slots[tok] = (flat_bt[offs[tok_seq] + blk] * block_size + p % block_size).astype(np.int32)
         if all_logits:          # every token row gets logits (tp_forward)
             row_dst = np.arange(T, dtype=np.int32)
         else:
@@ -272,10 +290,13 @@ class StepMeta:
 
         def subset(mask):
             idx = np.nonzero(mask)[0]
-            bt_ld = max([len(block_tables[i]) for i in idx] + [bt_width, 1])
+            rl = lens[idx]
+            bt_ld = max(int(rl.max()) if len(idx) else 0, bt_width, 1)
             bt = np.full((len(idx), bt_ld), -1, dtype=np.int32)
-            for r, i in enumerate(idx):
-                bt[r, :len(block_tables[i])] = block_tables[i]
+            if len(idx):
+                cols = np.arange(bt_ld)
+                valid = cols[None, :] < rl[:, None]
+                bt[valid] = flat_bt[(offs[idx][:, None] + cols[None, :])[valid]]
             return idx, starts[idx], qlen[idx], ctx[idx], bt
 
         d_idx, d_qs, d_ql, d_ctx, d_bt = subset(is_dec)
@@ -287,9 +308,13 @@ class StepMeta:
         parts = [ids, pos, slots, row_dst, d_qs, d_ql, d_ctx, d_bt.ravel(), d_order, p_qs, p_ql,
                  p_ctx, p_bt.ravel(), work.ravel()]
         flat = np.concatenate(parts).astype(np.int32)
-        host = torch.from_numpy(flat)
-        if pinned and torch.device(device).type == "cuda":
-            host = host.pin_memory()
+        if staging is not None and staging.numel() >= flat.size:
+            host = staging[: flat.size]
+            host.numpy()[:] = flat
+        else:
+            host = torch.from_numpy(flat)
+            if pinned and torch.device(device).type == "cuda":
+                host = host.pin_memory()
         if dest is not None:
             if dest.numel() != flat.size:
                 raise ValueError("metadata layout differs from the destination buffer")
@@ -533,6 +558,12 @@ class DecodeGraph:
                            [[0]] * n, [1] * n, block_size, group, dm.device,
                            bt_width=bt_width)
         self.dest = self.md.buf
+        # two pinned host buffers, alternated by staging(): a step's metadata
+        # copy is issued from one while the previous step's may still be reading
+        # the other
+        self._staging = [torch.empty(self.dest.numel(), dtype=torch.int32).pin_memory()
+                         for _ in range(2)]
+        self._turn = 0
         # one eager run (sizes the scratch arenas and sets kernel attributes
         # outside the capture) on a throw-away one-block pool per layer, so the
         # dummy batch never writes into the live cache; the capture itself
@@ -548,6 +579,11 @@ class DecodeGraph:
             dm.forward(self.md, kv_pools, sample=True, attn_max_ctx=max_ctx)
         torch.cuda.synchronize(dm.device)
         self.gen = dm.generation()
+
+    def staging(self) -> torch.Tensor:
+        """The next pinned host buffer for a ``StepMeta(..., dest=self.dest)``."""
+        self._turn ^= 1
+        return self._staging[self._turn]
 
     def stale(self) -> bool:
         return self.gen != self.dm.generation()

@@ -29,6 +29,43 @@ class Status(Enum):
     FINISHED = "finished"
 
 
+class TokenView:
+    """Read-only sequence over ``prompt + outputs`` (optionally its first
+    ``limit`` tokens) supporting ``len``, indexing and slicing; what the block
+    manager reads of a sequence, without building the whole list every step."""
+
+    __slots__ = ("_p", "_o", "_n")
+
+    def __init__(self, prompt: list[int], outputs: list[int], limit: int | None = None):
+        self._p, self._o = prompt, outputs
+        total = len(prompt) + len(outputs)
+        self._n = total if limit is None else max(0, min(limit, total))
+
+    def __len__(self) -> int:
+        return self._n
+
+    def __getitem__(self, k):
+        if isinstance(k, slice):
+            a, b, step = k.indices(self._n)
+            if step != 1:
+                return list(self)[k]
+            np_ = len(self._p)
+            if b <= np_:
+                return self._p[a:b]
+            if a >= np_:
+                return self._o[a - np_:b - np_]
+            return self._p[a:] + self._o[:b - np_]
+        if k < 0:
+            k += self._n
+        if not 0 <= k < self._n:
+            raise IndexError(k)
+        np_ = len(self._p)
+        return self._p[k] if k < np_ else self._o[k - np_]
+
+    def __iter__(self):
+        return iter(self[0:self._n])
+
+
 @dataclass
 class Request:
     prompt_token_ids: list[int]
@@ -49,8 +86,17 @@ class Request:
     def all_token_ids(self) -> list[int]:
         return self.prompt_token_ids + self.output_token_ids
 
+    def token_view(self, limit: int | None = None) -> "TokenView":
+        """``all_token_ids()[:limit]`` as a read-only view (no copy of the
+        whole sequence; slices are built on demand)."""
+        return TokenView(self.prompt_token_ids, self.output_token_ids, limit)
+
     def context_len(self) -> int:
         return len(self.prompt_token_ids) + len(self.output_token_ids)
+
+    def last_token_id(self) -> int:
+        """``all_token_ids()[-1]`` without building the list."""
+        return self.output_token_ids[-1] if self.output_token_ids else self.prompt_token_ids[-1]
 
 
 @dataclass
@@ -78,14 +124,14 @@ class Scheduler:
     def _reserve_decode_slot(self, req: Request) -> bool:
         """Reserve one KV slot for ``req``; False if ``req`` got preempted."""
         try:
-            self.bm.append_slot(req.block_table, req.all_token_ids())
+            self.bm.append_slot(req.block_table, req.token_view())
             return True
         except OutOfBlocks:
             pass
         if self._preempt_youngest() is req:
             return False
         try:
-            self.bm.append_slot(req.block_table, req.all_token_ids())
+            self.bm.append_slot(req.block_table, req.token_view())
             return True
         except OutOfBlocks:
             self._preempt(req)
