@@ -147,7 +147,8 @@ int tb_linear_static_scratch(const void* x, int ldx, const void* w, int ldw, int
  * (= block*block_size + offset).
  * Replaces q/k/v F.linear + _rope + PagedKVCache.write
  * (src/tinybatch/model.py:119-128, kv_cache.py:25-38,
- *  tensor_parallel.py:92-97).  bn must be a multiple of hd. */
+ *  tensor_parallel.py:92-97).  bn must be a multiple of hd; rope_cos and
+ * rope_sin 16-byte aligned. */
 int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const void* bias,
                    int M, int K, int n_q_heads, int n_kv_heads, int head_dim,
                    const float* sq, int sq_parts, int sq_ld, float inv_d, float eps,

@@ -128,6 +128,8 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
     return arg_err("null pointer");
   if (ld_q < n_q_heads * head_dim || ld_q % 8 || block_size <= 0 || max_pos <= 0)
     return arg_err("ld_q / block_size / max_pos");
+  if (reinterpret_cast<uintptr_t>(rope_cos) % 16 || reinterpret_cast<uintptr_t>(rope_sin) % 16)
+    return arg_err("rope_cos / rope_sin must be 16-byte aligned");
   const int N = (n_q_heads + 2 * n_kv_heads) * head_dim;
   GemmArgs g = base_args(M, N, K, splits, sq, sq_parts, sq_ld, inv_d, eps);
   g.out = q_out;

@@ -853,11 +853,18 @@ __device__ __forceinline__ void finish_qkv(const GemmArgs& g, const RowStage& rw
       const float2 bl0 = bf16x2_to_float2(bl2.x), bl1 = bf16x2_to_float2(bl2.y);
       const float2 bh0 = bf16x2_to_float2(bh2.x), bh1 = bf16x2_to_float2(bh2.y);
       const float bl[4] = {bl0.x, bl0.y, bl1.x, bl1.y}, bh[4] = {bh0.x, bh0.y, bh1.x, bh1.y};
-      float4 lo4[4], hi4[4];
+      // every input of the four rows first (shared sums, rotary cos/sin as
+      // one 16-byte load each), so their latencies overlap
+      float4 lo4[4], hi4[4], cs4[4], sn4[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         lo4[j] = stage_sum(smem, nsrc, nslot, 2 * lp, r0 + 32 * j, i);
         hi4[j] = stage_sum(smem, nsrc, nslot, 2 * lp + 1, r0 + 32 * j, i);
+        if (rotate) {
+          const size_t f = (size_t)rw.pos[r0 + 32 * j] * half + c_lo;
+          cs4[j] = *reinterpret_cast<const float4*>(g.rope_cos + f);
+          sn4[j] = *reinterpret_cast<const float4*>(g.rope_sin + f);
+        }
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -868,15 +875,15 @@ __device__ __forceinline__ void finish_qkv(const GemmArgs& g, const RowStage& rw
         const float4 a = lo4[j], b = hi4[j];
         const float rs = rw.rs[row];
         const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+        const float cv[4] = {cs4[j].x, cs4[j].y, cs4[j].z, cs4[j].w};
+        const float sv[4] = {sn4[j].x, sn4[j].y, sn4[j].z, sn4[j].w};
         float o1[4], o2[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float x1 = av[e] * rs + bl[e], x2 = bv[e] * rs + bh[e];
           if (rotate) {
-            const size_t f = (size_t)rw.pos[row] * half + c_lo + e;
-            const float c = g.rope_cos[f], s = g.rope_sin[f];
-            o1[e] = x1 * c - x2 * s;
-            o2[e] = x2 * c + x1 * s;
+            o1[e] = x1 * cv[e] - x2 * sv[e];
+            o2[e] = x2 * cv[e] + x1 * sv[e];
           } else {
             o1[e] = x1;
             o2[e] = x2;

@@ -60,14 +60,31 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* logits, int ld
   const bool vec = (ld % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) % 16 == 0);
   if (vec) {
     const int n4 = N / 4;
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-      const float4 v = reinterpret_cast<const float4*>(row)[i];
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int stride = blockDim.x;
+    int i = threadIdx.x;
+    // four loads in flight per thread, then the comparisons in index order
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = __ldcs(r4 + i + k * stride);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int b = 4 * (i + k * stride);
+        better(bv, bi, v[k].x, b);
+        better(bv, bi, v[k].y, b + 1);
+        better(bv, bi, v[k].z, b + 2);
+        better(bv, bi, v[k].w, b + 3);
+      }
+    }
+    for (; i < n4; i += stride) {
+      const float4 v = r4[i];
       better(bv, bi, v.x, 4 * i);
       better(bv, bi, v.y, 4 * i + 1);
       better(bv, bi, v.z, 4 * i + 2);
       better(bv, bi, v.w, 4 * i + 3);
     }
-    for (int i = 4 * n4 + threadIdx.x; i < N; i += blockDim.x) better(bv, bi, row[i], i);
+    for (int j = 4 * n4 + threadIdx.x; j < N; j += blockDim.x) better(bv, bi, row[j], j);
   } else {
     for (int i = threadIdx.x; i < N; i += blockDim.x) better(bv, bi, row[i], i);
   }
