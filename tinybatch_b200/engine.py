@@ -166,7 +166,7 @@ class LLMEngine:
         ids, pos, slices, tables, ctx = self.build_batch(batch)
         greedy = all(r.temperature <= 0.0 for r in ordered)
         if self.cuda_graphs and greedy and not batch.prefill:
-            g = self.decode_graph(len(ordered))
+            g = self.decode_graph(len(ordered), sum(ctx))
             md = StepMeta(ids, pos, slices, tables, ctx, self.cfg.block_size,
                           self.model.cfg.n_heads // self.model.cfg.n_kv_heads, self.device,
                           bt_width=self._bt_width, dest=g.dest, staging=g.staging())
@@ -200,12 +200,16 @@ class LLMEngine:
             outputs.append(StepOutput(req.req_id, tok, delta, finished, req))
         return outputs
 
-    def decode_graph(self, n: int) -> DecodeGraph:
-        """The captured decode step for ``n`` sequences (captured on first use)."""
+    def decode_graph(self, n: int, ctx_total: int | None = None) -> DecodeGraph:
+        """The captured decode step for ``n`` sequences (captured on first
+        use; its split-KV size is chosen for ``ctx_total``, by default the
+        running requests' summed context length)."""
         g = self._graphs.get(n)
         if g is None or g.stale():
+            if ctx_total is None:
+                ctx_total = sum(r.context_len() for r in self.scheduler.running) or None
             g = DecodeGraph(self.model.dm, self.kv_cache.pools, n, self._bt_width,
-                            self.cfg.max_model_len, self.cfg.block_size)
+                            self.cfg.max_model_len, self.cfg.block_size, ctx_total=ctx_total)
             self._graphs[n] = g
         return g
 

@@ -116,15 +116,17 @@ ATTN_MAX_SPLIT = 8192
 
 def decode_split_tokens(n_seqs: int, n_kv: int, ctx_total: int, max_ctx: int,
                         slots: int = ATTN_SLOTS) -> int:
-    """Keys per split-KV piece of a decode attention launch.  With at least
-    two CTAs per resident slot from (sequence, kv head) pairs alone, every
-    pair runs as one CTA (dispatched longest first, no merge); otherwise the
-    keys are cut so that about 2 x slots CTAs run.  A multiple of 16 in
+    """Keys per split-KV piece of a decode attention launch.  Measured on the
+    14B decode shards (TP 1-8): fastest when the launch has about 0.6 CTAs
+    per resident slot.  So when the (sequence, kv head) pairs alone reach
+    that, every pair runs as one CTA (dispatched longest first, no merge);
+    otherwise the keys are cut to about that many CTAs.  A multiple of 16 in
     [256, 8192]."""
-    if n_seqs * n_kv >= 2 * slots:
+    target = 0.6 * slots
+    if n_seqs * n_kv >= target:
         split = max_ctx
     else:
-        split = -(-ctx_total * n_kv // (2 * slots))
+        split = -(-ctx_total * n_kv // int(target))
     return min(ATTN_MAX_SPLIT, max(256, -(-split // 16) * 16))
 
 
@@ -458,10 +460,12 @@ class DeviceModel:
         return N.l2_next(w, plan[1], self.l2_prefetch_bytes)
 
     def forward(self, md: StepMeta, kv_pools: list[torch.Tensor], compute_logits: bool = True,
-                sample: bool = False, attn_max_ctx: int | None = None):
+                sample: bool = False, attn_max_ctx: int | None = None,
+                attn_split: int | None = None):
         """Launch the forward.  ``attn_max_ctx`` sizes the decode attention
         grid (default: this batch's longest context); a CUDA graph passes its
-        bound so one capture serves every context length up to it.
+        bound so one capture serves every context length up to it, and
+        ``attn_split`` its split-KV size.
 
         Every GEMM whose epilogue is followed by another weight-streaming GEMM
         asks for the next weight to be warmed into L2 (o_proj -> gate/up ->
@@ -496,7 +500,7 @@ class DeviceModel:
             qrow = W.n_q * hd * 2
             if md.n_dec:
                 mc = attn_max_ctx or md.dec_max_ctx
-                split = self.split_tokens or decode_split_tokens(
+                split = attn_split or self.split_tokens or decode_split_tokens(
                     md.n_dec, W.n_kv, md.n_dec * mc if attn_max_ctx else md.dec_ctx_sum, mc)
                 self._run(
                     "attention_decode", dec_ctx * kv_row + 2 * md.dec_tokens * qrow,
@@ -549,10 +553,14 @@ class DecodeGraph:
     copies it there, then replays: every kernel of the step, no host work."""
 
     def __init__(self, dm: DeviceModel, kv_pools, n: int, bt_width: int, max_ctx: int,
-                 block_size: int):
+                 block_size: int, ctx_total: int | None = None):
+        """``ctx_total``: the summed context length of a typical batch (the
+        one being captured for): the split-KV size is chosen for it."""
         self.dm, self.pools = dm, kv_pools
         self.n, self.bt_width, self.max_ctx = n, bt_width, max_ctx
         group = dm.cfg.n_heads // dm.cfg.n_kv_heads
+        self.split = dm.split_tokens or decode_split_tokens(
+            n, dm.w.n_kv, ctx_total if ctx_total else n * max_ctx, max_ctx)
         # a valid dummy batch: every sequence has one token at position 0 in block 0
         self.md = StepMeta([0] * n, [0] * n, [(i, i + 1) for i in range(n)],
                            [[0]] * n, [1] * n, block_size, group, dm.device,
@@ -571,12 +579,13 @@ class DecodeGraph:
         p0 = kv_pools[0]
         dummy = [torch.zeros((1,) + tuple(p0.shape[1:]), dtype=p0.dtype, device=p0.device)
                  for _ in kv_pools]
-        dm.forward(self.md, dummy, sample=True, attn_max_ctx=max_ctx)
+        dm.forward(self.md, dummy, sample=True, attn_max_ctx=max_ctx, attn_split=self.split)
         torch.cuda.synchronize(dm.device)
         del dummy
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            dm.forward(self.md, kv_pools, sample=True, attn_max_ctx=max_ctx)
+            dm.forward(self.md, kv_pools, sample=True, attn_max_ctx=max_ctx,
+                       attn_split=self.split)
         torch.cuda.synchronize(dm.device)
         self.gen = dm.generation()
 
