@@ -208,8 +208,8 @@ int tb_comm_destroy(void* comm);
  *   h += sum over ranks of (x_r . w_r^T)   (x_r, w_r: this rank's K shard)
  * then hg / sq_out as tb_row_linear_residual.  Each CTA pushes its bf16
  * partial tile to the peers over NVLink (two_shot = 0: to every rank, which
- * sums the partials in rank order; two_shot = 1: to the column's owner, which
- * sums and broadcasts), so h stays identical on all ranks.  Every rank must
+ * sums the partials in rank order; two_shot = 1: each row to the row's owner
+ * rank, which sums and broadcasts), so h stays identical on all ranks.  Every rank must
  * make the same calls (same M, N, K, bn, splits, site) in the same order.
  * A partner that does not arrive within 5 s sets TB_STATUS_PEER_TIMEOUT.
  * Replaces allreduce(F.linear(attn, Wo)) / allreduce(F.linear(act, Wd)) + the

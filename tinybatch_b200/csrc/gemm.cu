@@ -400,13 +400,14 @@ __device__ __forceinline__ void exchange_flags(const CommDev& c, FS send_flag, F
 //
 //   one-shot  every rank pushes its bf16 partial of the CTA's columns to
 //             every rank; each rank sums the world partials in rank order
-//   two-shot  every rank pushes each column's partial to the column's owner
-//             (rank n / (N / world)); the owner sums them in rank order and
-//             pushes the bf16 sum to every rank
+//   two-shot  every rank pushes each row's partial to the row's owner (rank
+//             row_in_tile * world / 128, so every CTA owns an equal share of
+//             its tile); the owner sums them in rank order and pushes the
+//             bf16 sum to every rank
 // Every rank then adds the same bf16 values to its replicated fp32 residual,
 // so h stays bit-identical on all ranks.  A CTA's partners are the CTAs
 // with the same index on the other ranks; "delivered" flags carry the call's
-// epoch (release stores after a system fence; acquire loads, bounded wait).
+// epoch (release stores by parallel lanes; acquire loads, bounded waits).
 //
 // Exchange layout: [tile][16-column unit][half][128 rows][8 columns] bf16, the
 // epilogue's own thread order (thread = row), so one warp store or load
@@ -425,7 +426,7 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
   // plane: every tile of a max_rows x n_cols output, padded to whole tiles
   const size_t plane = (size_t)((c.max_rows + BM - 1) / BM) * BM * (size_t)(c.n_cols + 256);
   const int cta = flag_slot;   // this CTA's (tile's) flags: same index on every rank
-  const int per_owner = N / c.world;
+  const int row_owner = row * c.world / BM;   // two-shot: the rank that reduces this row
   const bool leader = threadIdx.x == 64;
   const bool flag_warp = (threadIdx.x >> 5) == 2;   // the first epilogue warp
   constexpr int U = BN / 16;
@@ -452,7 +453,7 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
     acc.load16(u, u / n_own, v);
     if (!valid) continue;
     if (c.two_shot) {
-      put16(rs_at(n / per_owner, c.rank), u, v);
+      put16(rs_at(row_owner, c.rank), u, v);
     } else {
       for (int p = 0; p < c.world; ++p) put16(rs_at(p, c.rank), u, v);
     }
@@ -512,12 +513,12 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
     return ss;
   }
 
-  // 2'. owners reduce their columns and broadcast the bf16 sums
+  // 2'. owners reduce their rows and broadcast the bf16 sums
   const size_t ag_off = (size_t)par * plane;
   for (int u = own; u < U; u += n_own) {
     const int n = tn * BN + u * 16;
     if (n >= N) break;
-    if (!valid || n / per_owner != c.rank) continue;
+    if (!valid || row_owner != c.rank) continue;
     float v[16];
     sum_partials(u, v);
     for (int p = 0; p < c.world; ++p) put16(c.ag[p] + ag_off, u, v);
