@@ -31,6 +31,9 @@ _SIGS = {
                           c_void_p, c_int, c_int, c_float, c_float,
                           c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p,
                           c_void_p]),
+    "tb_linear_static_scratch": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
+                                         c_void_p, c_int, c_int, c_float, c_float,
+                                         c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "tb_qkv_rope_kv": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
                                c_int, c_int, c_int, c_void_p, c_int, c_int, c_float, c_float,
                                c_void_p, c_void_p, c_int, c_void_p, c_void_p,
