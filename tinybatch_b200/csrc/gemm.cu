@@ -944,6 +944,10 @@ __device__ __forceinline__ void finish(const GemmArgs& g, const RowStage& rw, co
     finish_linear<BN, EPI>(g, rw, smem, nsrc, nslot, tm, tn, p0, p_end, step, t);
 }
 
+// Split-K GEMM: one CTA per (tile, k-slice).  With scratch the slices park
+// fp32 partials in global memory and the last to arrive finishes the tile;
+// without it a tile's slices form one cluster and push their partials into
+// the owners' shared memory.
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -966,7 +970,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   int* row_dst = row_slot + BM;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mode = g.splits == 1 ? SPLIT_NONE : (g.ws != nullptr ? SPLIT_GLOBAL : SPLIT_CLUSTER);
+  // split-K only: launches without it run gemm_persistent_kernel
+  const int mode = g.ws != nullptr ? SPLIT_GLOBAL : SPLIT_CLUSTER;
 
   // grouped raster: m fastest inside a group of group_m row tiles
   const int tile = mode == SPLIT_CLUSTER ? (int)blockIdx.x / g.splits : (int)blockIdx.x;
@@ -1109,8 +1114,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     mbar_wait(done, 0);
     tc_fence_after();
     if (threadIdx.x == 64) trace_at(g, TR_ACC_READY);
-    bool run = true;
-    if (mode == SPLIT_GLOBAL) {
+    bool run;
+    {
       const size_t tile_lin = (size_t)tm * g.tiles_n + tn;
       float* ws_tile = g.ws + tile_lin * g.splits * BN * BM;
       float* mine = ws_tile + (size_t)z * BN * BM + row;
@@ -1138,8 +1143,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre, blockIdx.x, nullptr);
         store_row_sumsq(g, tm, tn, row, ss);
       } else {
-        if (mode == SPLIT_GLOBAL) stage_global<BN>(acc, tu, smem, nslot, row);
-        else stage_acc<BN>(acc, tu, 1, 0, smem, nslot, row, false);
+        stage_global<BN>(acc, tu, smem, nslot, row);
         epi_bar();   // staged chunks and per-row values visible to every finisher thread
         float ss[4] = {0.f, 0.f, 0.f, 0.f};
         finish<BN, EPI>(g, rw, smem, 1, nslot, tm, tn, 0, 1 << 30, 1, t, &fpre, ss);
@@ -1502,6 +1506,10 @@ int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb,
     return arg_err("cluster split-K supports at most 8 splits");
   if (g.splits > 1 && (g.ws == nullptr) != (g.counters == nullptr))
     return arg_err("split-K scratch pointers");
+  if (g.splits == 1) {   // no split-K: the persistent kernel, no scratch
+    g.ws = nullptr;
+    g.counters = nullptr;
+  }
   g.tiles_m = (g.M + BM - 1) / BM;
   g.tiles_n = (g.N + bn - 1) / bn;
   if (g.group_m <= 0) g.group_m = 16;

@@ -63,13 +63,14 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* logits, int ld
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int stride = blockDim.x;
     int i = threadIdx.x;
-    // four loads in flight per thread, then the comparisons in index order
-    for (; i + 3 * stride < n4; i += 4 * stride) {
-      float4 v[4];
+    // eight loads in flight per thread (64 KiB per CTA: one CTA per row has
+    // to pull its row at ~1/128 of the HBM bandwidth), then the comparisons
+    for (; i + 7 * stride < n4; i += 8 * stride) {
+      float4 v[8];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) v[k] = __ldcs(r4 + i + k * stride);
+      for (int k = 0; k < 8; ++k) v[k] = __ldcs(r4 + i + k * stride);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 8; ++k) {
         const int b = 4 * (i + k * stride);
         better(bv, bi, v[k].x, b);
         better(bv, bi, v[k].y, b + 1);
