@@ -28,6 +28,20 @@ def test_plans_respect_fit_and_k():
         assert s <= -(-K // 64)
 
 
+def test_plans_follow_measured_rankings():
+    """Decode shapes (M = 128) whose (bn, splits) were timed on a B200 in
+    graph replay: the planner must pick the faster of each measured pair.
+    o_proj TP=1: (128, 3) 16.1 us vs (256, 6) 18.1; down TP=1: (128, 3) 32.0
+    vs (256, 6) 33.4; o_proj TP=4: (128, 3) 9.9 vs (64, 1) 13.0; down TP=4:
+    (128, 3) 13.5 vs (64, 1) 22.8; down at M = 4096: (192, 1) 515 vs (256, 2)
+    598."""
+    assert plan_gemm(128, 5120, 5120) == (128, 3)
+    assert plan_gemm(128, 5120, 13824) == (128, 3)
+    assert plan_gemm(128, 5120, 1280) == (128, 3)
+    assert plan_gemm(128, 5120, 3456) == (128, 3)
+    assert plan_gemm(4096, 5120, 13824) == (192, 1)
+
+
 def test_row_parts():
     assert ops.row_parts(5120, 256, 6) == 120
     assert ops.row_parts(5120, 256, 6, "global") == 20

@@ -659,15 +659,34 @@ __device__ __forceinline__ int fin_piece(int t) { return (t & 31) >> 3; }
 __device__ __forceinline__ int fin_row(int t) { return (t & 7) + 8 * (t >> 5); }
 //
 // Residual inputs of one chunk for a finisher thread: its 4 rows of h (4
-// float4) and 4 bf16 of g_next.  The first chunk's are loaded before the
-// accumulator is ready; every later chunk's one chunk ahead.
-struct FinPre {
+// float4) and 4 bf16 of g_next.
+struct FinIn {
   float4 h[4];
   uint2 g;
 };
 
+// The inputs of the first n (<= FIN_PRE) chunks a finisher thread handles,
+// loaded while the main loop runs.  A cluster member owns at most
+// ceil(pairs / splits) chunks (3 for bn 128 x 3 and bn 256 x 6), so they all
+// arrive in one round trip instead of one per chunk; chunks beyond these
+// are loaded one chunk ahead.
+constexpr int FIN_PRE = 4;
+struct FinPre {
+  FinIn c[FIN_PRE];
+  int n;
+  // c[k] for a k < FIN_PRE known only at run time (selects: the array stays
+  // in registers)
+  __device__ __forceinline__ FinIn at(int k) const {
+    FinIn r = c[0];
+#pragma unroll
+    for (int j = 1; j < FIN_PRE; ++j)
+      if (k == j) r = c[j];
+    return r;
+  }
+};
+
 __device__ __forceinline__ void load_fin_inputs(const GemmArgs& g, int tm, int r0, int n,
-                                                FinPre& p) {
+                                                FinIn& p) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int m = tm * BM + r0 + 32 * j;
@@ -678,18 +697,25 @@ __device__ __forceinline__ void load_fin_inputs(const GemmArgs& g, int tm, int r
 }
 
 template <int BN>
-__device__ __forceinline__ void fin_prefetch(const GemmArgs& g, int tm, int tn, int own, int t,
-                                             FinPre& p) {
-  if (own < BN / 16 && tn * BN + own * 16 < g.N)
-    load_fin_inputs(g, tm, fin_row(t), tn * BN + own * 16 + 4 * fin_piece(t), p);
+__device__ __forceinline__ void fin_prefetch(const GemmArgs& g, int tm, int tn, int own, int step,
+                                             int t, FinPre& p) {
+  p.n = 0;
+#pragma unroll
+  for (int k = 0; k < FIN_PRE; ++k) {
+    const int u = own + k * step;
+    if (u < BN / 16 && tn * BN + u * 16 < g.N) {
+      load_fin_inputs(g, tm, fin_row(t), tn * BN + u * 16 + 4 * fin_piece(t), p.c[k]);
+      p.n = k + 1;
+    }
+  }
 }
 
 // h += acc; hg = bf16(h * g_next) (and its copy in row dst of hg2), for the
 // chunks p0, p0 + step, ... below p_end (staging slots 0, 1, ...); the row
 // sums of the new h^2 are added to ss (this thread's 4 rows).  One rolled
 // loop over the chunks (the epilogue code runs from a cold instruction cache:
-// compact code matters), each chunk's inputs loaded one chunk ahead; the first
-// chunk's come from `pre` when given.
+// compact code matters); the inputs of the first pre->n chunks come from
+// `pre` when given, every later chunk's are loaded one chunk ahead.
 template <int BN>
 __device__ __forceinline__ void finish_resid(const GemmArgs& g, const RowStage& rw,
                                              const uint8_t* smem, int nsrc, int nslot, int tm,
@@ -697,17 +723,18 @@ __device__ __forceinline__ void finish_resid(const GemmArgs& g, const RowStage& 
                                              const FinPre* pre, float* ss) {
   const int U = min(BN / 16, p_end);
   const int i = fin_piece(t), r0 = fin_row(t);
-  FinPre cur;
-  if (p0 < U && tn * BN + p0 * 16 < g.N) {
-    if (pre != nullptr) cur = *pre;
-    else load_fin_inputs(g, tm, r0, tn * BN + p0 * 16 + 4 * i, cur);
-  }
+  const int npre = pre != nullptr ? pre->n : 0;
+  FinIn cur;
+  if (npre > 0) cur = pre->c[0];
+  else if (p0 < U && tn * BN + p0 * 16 < g.N)
+    load_fin_inputs(g, tm, r0, tn * BN + p0 * 16 + 4 * i, cur);
   int lp = 0;
 #pragma unroll 1
   for (int u = p0; u < U && tn * BN + u * 16 < g.N; u += step, ++lp) {
     const int un = u + step;
-    FinPre nxt;
-    if (un < U && tn * BN + un * 16 < g.N)
+    FinIn nxt;
+    if (lp + 1 < npre) nxt = pre->at(lp + 1);
+    else if (un < U && tn * BN + un * 16 < g.N)
       load_fin_inputs(g, tm, r0, tn * BN + un * 16 + 4 * i, nxt);
     const int n = tn * BN + u * 16 + 4 * i;
     const float2 ga = bf16x2_to_float2(cur.g.x), gb = bf16x2_to_float2(cur.g.y);
@@ -1072,14 +1099,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const RowStage rw{row_rs, row_pos, row_slot, row_dst};
 
   ResidPre pre;     // tensor-parallel residual: one row per thread
-  FinPre fpre;      // finisher: first chunk of each of its rows
+  FinPre fpre;      // finisher: inputs of its first chunks
   if (warp >= 2) {
     pdl_wait();   // the epilogue reads and writes buffers earlier kernels use
     // inputs that do not depend on the accumulator load under the main loop
     stage_rows<EPI>(g, rw, tm, row);
     if constexpr (EPI == EPI_RESID) {
       if (tp) resid_prefetch<BN>(g, tm, tn, row, mode == SPLIT_CLUSTER ? z : 0, S, pre);
-      else fin_prefetch<BN>(g, tm, tn, mode == SPLIT_CLUSTER ? z : 0, t, fpre);
+      else fin_prefetch<BN>(g, tm, tn, mode == SPLIT_CLUSTER ? z : 0, S, t, fpre);
     }
   }
   if (mode == SPLIT_CLUSTER) {

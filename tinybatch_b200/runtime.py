@@ -69,9 +69,11 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
     """Tile width and cluster split-K factor for C[M,N] = A[M,K] B[N,K]^T.
 
     Time model, fitted to device timelines of the decode shapes on B200:
-    a CTA streams its B slice plus ~35% of its A slice (the rest hits L2) at
-    min(50 GB/s, 6 TB/s / active CTAs), or is bound by its share of the
-    tensor pipe (~10.8 TFLOP/s per SM); its epilogue then costs ~1.5 us of
+    a CTA streams its B slice from HBM at min(50 GB/s, 6 TB/s / active
+    CTAs), takes its A and B boxes into shared memory at ~95 GB/s (A comes
+    from L2 but still passes through the SM's copy engine: narrow tiles pay
+    for it), or is bound by its share of the tensor pipe (~10.8 TFLOP/s per
+    SM), whichever is slowest; its epilogue then costs ~1.5 us of
     launch and prologue, ~0.9 us per 16-column chunk it finishes and, with
     split-K, one cluster barrier (~1.3 us) plus the partial chunks it stores
     into the other members' shared memory at ~25 GB/s.  A launch with more
@@ -91,19 +93,20 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
                 continue
             ctas = tiles * s
             k_it = -(-num_k // s)
-            cta_bytes = k_it * 64 * 2 * (bn + 0.35 * 128)
+            b_bytes = k_it * 64 * 2 * bn
+            ab_bytes = b_bytes + k_it * 64 * 2 * 128
             cta_flops = 2.0 * 128 * bn * 64 * k_it
             epi = 1.5e-6 + 0.9e-6 * (bn / 16) / s
             if s > 1:
                 epi += 1.3e-6 + (bn * 128 * 4 * (s - 1) / s) / 25e9
             if tiles <= cap[s - 1]:
                 bw = min(50e9, 6.0e12 / ctas)
-                t = max(cta_bytes / bw, cta_flops / 10.8e12) + epi
+                t = max(b_bytes / bw, ab_bytes / 95e9, cta_flops / 10.8e12) + epi
             else:     # several waves of fully busy SMs (39 GB/s each); a tail
                 # wave costs a whole wave (and, in a fused all-reduce, another
                 # exchange round trip)
                 waves = -(-ctas // (cap[s - 1] * s))
-                t = waves * (max(cta_bytes / 39e9, cta_flops / 10.8e12) + epi)
+                t = waves * (max(b_bytes / 39e9, ab_bytes / 95e9, cta_flops / 10.8e12) + epi)
             if best is None or t < best[0]:
                 best = (t, bn, s)
     return best[1], best[2]
