@@ -11,6 +11,13 @@ decoding sequence) -> forward -> sample -> append / finish.  Differences:
   token ids come back (4 bytes per sequence);
 * requests can be given as token ids (``add_request_ids``); a tokenizer is
   only needed for text prompts;
+* ``EngineConfig.overlap_steps``: once the batch is a steady greedy decode
+  batch, ``step`` queues the next decode step on the device (its token ids
+  copied there from this step's argmax) before reading this step's tokens
+  back, so the host's scheduling and output handling run while the GPU
+  computes.  Every request produces the same tokens as without it; a
+  sequence that stops at step k had step k+1 computed for nothing (its
+  output is dropped, its blocks freed);
 * a prompt whose length is a multiple of the block size gets the block for
   its first decode token here.  The reference scheduler reserves the slot
   *after* the token being written (``append_slot`` sees the token list that
@@ -33,7 +40,10 @@ from .config import EngineConfig
 from .kv_cache import PagedKVCache
 from .model import Qwen2Paged
 from .runtime import DecodeGraph, StepMeta
-from .scheduler import Request, Scheduler
+from .scheduler import Request, Scheduler, Status
+
+# output slot of a token still being computed on the device (overlapped steps)
+PENDING = -1
 
 
 @dataclass
@@ -43,6 +53,16 @@ class StepOutput:
     text_delta: str
     finished: bool
     request: Request = field(repr=False)
+
+
+@dataclass
+class _InFlight:
+    """A decode step queued on the device whose tokens are not read yet."""
+    reqs: list            # the step's sequences, in batch order
+    slots: list           # index of each one's pending token in output_token_ids
+    host_ids: torch.Tensor    # pinned int32, filled by an asynchronous copy
+    done: torch.cuda.Event    # recorded after that copy
+    h2d_bytes: int
 
 
 class LLMEngine:
@@ -74,6 +94,9 @@ class LLMEngine:
                 self.eos_ids.add(im_end)
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
+        self._inflight: _InFlight | None = None
+        self._ids_host: list[torch.Tensor] = []
+        self._ids_turn = 0
 
     # ------------------------------------------------------------- API
 
@@ -158,7 +181,12 @@ class LLMEngine:
     def step(self, forced_tokens: list[int] | None = None) -> list[StepOutput]:
         """One engine iteration.  ``forced_tokens`` (one per scheduled
         sequence, prefill first) replaces the sampled tokens: teacher forcing
-        for parity tests."""
+        for parity tests.  With ``overlap_steps`` the outputs returned may be
+        those of a step queued by the previous call (see ``drain``)."""
+        if self.cfg.overlap_steps and forced_tokens is None:
+            return self._step_overlapped()
+        if self._inflight is not None:
+            return self.drain()
         batch = self.scheduler.schedule()
         if batch.is_empty():
             return []
@@ -196,6 +224,127 @@ class LLMEngine:
                         or req.context_len() >= self.cfg.max_model_len)
             delta = self.tokenizer.decode([tok], skip_special_tokens=True) if self.tokenizer else ""
             if finished:
+                self.scheduler.finish(req)
+            outputs.append(StepOutput(req.req_id, tok, delta, finished, req))
+        return outputs
+
+    # ------------------------------------------------- overlapped decode
+
+    def drain(self) -> list[StepOutput]:
+        """Outputs of the decode step still queued on the device, if any."""
+        f, self._inflight = self._inflight, None
+        return self._collect(f) if f is not None else []
+
+    def _step_overlapped(self) -> list[StepOutput]:
+        if self._inflight is None:
+            if not self._overlap_ready(None):
+                return self._plain_step()
+            self._inflight = self._launch(None)
+        nxt = self._launch(self._inflight) if self._overlap_ready(self._inflight) else None
+        out = self._collect(self._inflight)
+        if nxt is not None and all(r.status is Status.FINISHED for r in nxt.reqs):
+            self._collect(nxt)          # every sequence of it has stopped
+            nxt = None
+        self._inflight = nxt
+        return out
+
+    def _plain_step(self) -> list[StepOutput]:
+        overlap, self.cfg.overlap_steps = self.cfg.overlap_steps, False
+        try:
+            return self.step()
+        finally:
+            self.cfg.overlap_steps = overlap
+
+    def _overlap_ready(self, inflight: _InFlight | None) -> bool:
+        """Whether the next step is a decode of exactly the running sequences
+        (after ``inflight``, in its order) that the scheduler serves without
+        preempting: no waiting request, greedy sampling, no sequence stopping
+        for length at ``inflight``, a free block for every sequence that
+        starts one."""
+        sch = self.scheduler
+        if not self.cuda_graphs or self.cfg.enable_prefix_caching or sch.waiting:
+            return False
+        run = sch.running
+        if not run or any(r.status is not Status.RUNNING or r.temperature > 0.0 for r in run):
+            return False
+        if inflight is not None:
+            if len(inflight.reqs) != len(run) or any(a is not b for a, b in zip(inflight.reqs, run)):
+                return False
+            # capturing a graph runs a forward, which would overwrite the
+            # in-flight step's samples before they are fed
+            g = self._graphs.get(len(run))
+            if g is None or g.stale():
+                return False
+            lim = self.cfg.max_model_len
+            if any(len(r.output_token_ids) >= r.max_new_tokens or r.context_len() >= lim
+                   for r in run):
+                return False
+        # blocks the step may take: one where the next slot starts a block, one
+        # where build_batch extends a table (a prompt ending on a block boundary)
+        bs = self.cfg.block_size
+        need = sum((r.context_len() % bs == 0) + (len(r.block_table) * bs < r.context_len())
+                   for r in run)
+        return need <= self.block_manager.num_free()
+
+    def _launch(self, prev: _InFlight | None) -> _InFlight:
+        """Schedule and queue one decode step (graph replay) without waiting
+        for it.  With ``prev`` (the step queued before it, same sequences in
+        the same order) the token ids are ``prev``'s samples, copied on the
+        device; the host holds PENDING for them."""
+        batch = self.scheduler.schedule()
+        reqs = batch.decode
+        if batch.prefill or not reqs:
+            raise RuntimeError("overlapped step: a decode-only batch was expected")
+        n = len(reqs)
+        if prev is not None and (len(prev.reqs) != n or
+                                 any(a is not b for a, b in zip(prev.reqs, reqs))):
+            raise RuntimeError("overlapped step: the batch differs from the queued step's")
+        ids, pos, slices, tables, ctx = self.build_batch(batch)
+        g = self.decode_graph(n, sum(ctx))
+        md = StepMeta(ids, pos, slices, tables, ctx, self.cfg.block_size,
+                      self.model.cfg.n_heads // self.model.cfg.n_kv_heads, self.device,
+                      bt_width=self._bt_width, dest=g.dest, staging=g.staging())
+        dm = self.model.dm
+        if prev is not None:
+            g.md.ids.copy_(dm.next_ids[:n])
+        g.run(md)
+        if not self._ids_host or self._ids_host[0].numel() < n:
+            self._ids_host = [torch.empty(max(n, 64), dtype=torch.int32).pin_memory()
+                              for _ in range(2)]
+        host = self._ids_host[self._ids_turn]
+        self._ids_turn ^= 1
+        host[:n].copy_(dm.next_ids[:n], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        slots = []
+        for r in reqs:
+            slots.append(len(r.output_token_ids))
+            r.output_token_ids.append(PENDING)
+        self.last_batch = None
+        self.last_logits = None
+        return _InFlight(reqs, slots, host, done, md.h2d_bytes)
+
+    def _collect(self, f: _InFlight) -> list[StepOutput]:
+        """Wait for a queued step's tokens and apply them (append / finish) as
+        ``step`` does; sequences that stopped at an earlier step are skipped."""
+        f.done.synchronize()
+        toks = f.host_ids[: len(f.reqs)].tolist()
+        self.last_h2d_bytes = f.h2d_bytes
+        self.last_d2h_bytes = 4 * len(f.reqs)
+        now = time.perf_counter()
+        lim = self.cfg.max_model_len
+        outputs: list[StepOutput] = []
+        for req, idx, tok in zip(f.reqs, f.slots, toks):
+            if req.status is Status.FINISHED:
+                continue
+            req.output_token_ids[idx] = tok
+            if req.first_token_time is None:
+                req.first_token_time = now
+            finished = (tok in self.eos_ids or idx + 1 >= req.max_new_tokens
+                        or len(req.prompt_token_ids) + idx + 1 >= lim)
+            delta = self.tokenizer.decode([tok], skip_special_tokens=True) if self.tokenizer else ""
+            if finished:
+                del req.output_token_ids[idx + 1:]     # a later queued step's token
                 self.scheduler.finish(req)
             outputs.append(StepOutput(req.req_id, tok, delta, finished, req))
         return outputs
