@@ -221,6 +221,19 @@ int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int 
                                      int n_sites, int two_shot, int bn, int splits,
                                      const tb_l2_prefetch* next, void* stream);
 
+/* Greedy sampling over a vocabulary-parallel LM head: row m of logits
+ * (fp32, row pitch ld) holds this rank's n_local vocabulary columns, global
+ * columns col0 .. col0+n_local-1 (shards ordered by rank).  Every rank
+ * writes out[m] = the first index of the row's maximum over the whole
+ * vocabulary (torch.argmax of the full row; 0 when no value exceeds -inf).
+ * The candidates travel through the communicator like a row-parallel call:
+ * site is this call's place in the forward's n_sites, the same on every
+ * rank.  M <= max_rows and M <= max_ctas.  Replaces the replicated
+ * F.linear(h, lm_head) + argmax of the reference (tensor_parallel.py:117,
+ * engine.py:149-151) for the sampled rows. */
+int tb_argmax_vocab_parallel(void* comm, const float* logits, int ld, int M, int n_local,
+                             int col0, int* out, int site, int n_sites, void* stream);
+
 /* ------------------------------------------------------------- attention
  * Paged GQA attention reading K/V through block tables (no gather copy).
  *   q [*, Hq*hd] bf16 (ld_q), out [*, Hq*hd] bf16 (ld_out)

@@ -66,6 +66,8 @@ def test_host_only_entry_points(lib):
                                                None, None, None, None, 1, 100, 500, None, 0,
                                                None), "split_tokens"),
     (lambda lib: lib.tb_comm_begin_step(None, None), "communicator"),
+    (lambda lib: lib.tb_argmax_vocab_parallel(None, None, 512, 8, 256, 0, None, 96, 97, None),
+     "communicator"),
 ])
 def test_argument_errors_are_reported(lib, call, needle):
     rc = call(lib)

@@ -147,3 +147,92 @@ def test_run_tp_forward_matches_oracle(world):
     err = float((logits - ref).abs().max())
     assert err <= 2e-2, err
     assert stats["calls"] == 2 * cfg.n_layers
+
+
+def _sample_worker(rank, world, port, cfg, w, queue):
+    """One decode step of 24 sequences sampled on the device with the
+    vocabulary-parallel head, and the same step's full logits from the
+    replicated head; reports both."""
+    import datetime
+    import random
+
+    import torch.distributed as dist
+
+    from tinybatch_b200 import _native
+    from tinybatch_b200.comm import TPComm
+    from tinybatch_b200.model import Qwen2Paged
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    comm = TPComm(rank, world, dev, cfg.d_model, max_rows=256)
+    try:
+        model = Qwen2Paged.from_weights(cfg, w, device=dev, rank=rank, world=world, comm=comm,
+                                        max_tokens=64, max_seqs=64)
+        rng = random.Random(3)
+        ctx = [rng.randint(1, 200) for _ in range(24)]
+        tables, nb = [], 0
+        for c in ctx:
+            k = -(-c // 16)
+            tables.append(list(range(nb, nb + k)))
+            nb += k
+        cache = model.make_kv_cache(nb, 16)
+        g = torch.Generator(device=dev).manual_seed(5)
+        for pool in cache.pools:
+            pool.copy_(torch.randn(pool.shape, generator=g, device=dev).mul_(0.5))
+        ids = [rng.randrange(cfg.vocab_size) for _ in ctx]
+        md = model.metadata(ids, [c - 1 for c in ctx], [(i, i + 1) for i in range(24)], tables,
+                            ctx, 16)
+        full = model.dm.forward(md, cache.pools, sample=False).clone()
+        model.dm.forward(md, cache.pools, sample=True)
+        got = model.dm.next_ids[:24].clone()
+        torch.cuda.synchronize()
+        _native.raise_on_status(f"rank {rank}")
+        queue.put((rank, (full.cpu(), got.cpu())))
+    finally:
+        comm.close()
+        dist.destroy_process_group()
+
+
+def _vocab_parallel_case(world, tie):
+    from tinybatch_b200.config import ModelConfig
+    # vocabulary not divisible by the degree: ragged shards
+    cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=16, n_kv_heads=8, head_dim=64,
+                      d_ff=2048, vocab_size=509, rope_theta=1e6, rms_eps=1e-6,
+                      tie_embeddings=False, max_position=4096)
+    w = synthetic_weights(cfg, 11, dtype=torch.bfloat16)
+    if tie:
+        # every logit 0 except two equal ones in the first and the last shard:
+        # the answer is the smaller of the two when positive, else index 0
+        head = torch.zeros_like(w["lm_head.weight"])
+        v = torch.randn(cfg.d_model, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+        head[5] = v
+        head[cfg.vocab_size - 2] = v
+        w["lm_head.weight"] = head
+    return cfg, w
+
+
+@pytest.mark.parametrize("world,tie", [(2, False), (2, True), (4, False), (8, True)])
+def test_vocab_parallel_sampling(world, tie):
+    """Greedy ids from the vocabulary-parallel head + cross-rank argmax equal
+    torch.argmax of the replicated head's logits on every rank (exactly for
+    the constructed ties; wherever the top-2 gap is decisive otherwise)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} CUDA devices")
+    cfg, w = _vocab_parallel_case(world, tie)
+    res = _spawn(world, _sample_worker, (cfg, w), port=PORT + 60 + world + 10 * tie,
+                 timeout_s=300, collect_all=True)
+    full, ids0 = res[0]
+    for r in range(1, world):
+        assert torch.equal(res[r][1], ids0), f"rank {r} sampled different ids"
+    ref = full.argmax(-1).to(torch.int32)
+    if tie:
+        assert torch.equal(ids0, ref)
+        assert set(ids0.tolist()) <= {0, 5}
+    else:
+        top2 = full.topk(2, dim=-1).values
+        decisive = (top2[:, 0] - top2[:, 1]) > 1e-3
+        assert int(decisive.sum()) >= 20
+        assert torch.equal(ids0[decisive], ref[decisive])

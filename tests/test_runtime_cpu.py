@@ -42,6 +42,18 @@ def test_plans_follow_measured_rankings():
     assert plan_gemm(4096, 5120, 13824) == (192, 1)
 
 
+def test_vocab_shards_cover_the_vocabulary_in_rank_order():
+    from tinybatch_b200.runtime import vocab_shard
+    for V, t in [(152064, 8), (509, 2), (509, 8), (7, 8), (256, 4)]:
+        cols = []
+        for r in range(t):
+            c0, n = vocab_shard(V, r, t)
+            assert n >= 0 and c0 == min(r * -(-V // t), V)
+            cols += list(range(c0, c0 + n))
+        assert cols == list(range(V))
+    assert vocab_shard(152064, 3, 8) == (3 * 19008, 19008)
+
+
 def test_row_parts():
     assert ops.row_parts(5120, 256, 6) == 120
     assert ops.row_parts(5120, 256, 6, "global") == 20

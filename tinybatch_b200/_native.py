@@ -69,6 +69,8 @@ _SIGS = {
     "tb_embed": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p,
                          c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "tb_argmax": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "tb_argmax_vocab_parallel": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                         c_void_p, c_int, c_int, c_void_p]),
 }
 
 

@@ -86,6 +86,13 @@ class TPComm:
             bn, splits, N.pf_arg(next_weight), N.stream_ptr()),
             "tb_row_linear_allreduce_residual")
 
+    def argmax(self, logits, n_local: int, col0: int, out, *, site: int, n_sites: int) -> None:
+        """out[m] = torch.argmax over the whole vocabulary of row m, from this
+        rank's shard logits[:, :n_local] (global columns col0 ...)."""
+        N.check(N.load().tb_argmax_vocab_parallel(
+            self._ptr, N.ptr(logits), logits.stride(0), logits.shape[0], n_local, col0,
+            N.ptr(out), site, n_sites, N.stream_ptr()), "tb_argmax_vocab_parallel")
+
     def close(self, barrier: bool = True) -> None:
         if self.closed:
             return

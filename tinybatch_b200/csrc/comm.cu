@@ -33,6 +33,56 @@ __global__ void comm_step_kernel(uint32_t* state) {
   state[0] += 1u;
 }
 
+// Greedy sampling over a vocabulary-parallel LM head.  Row m of `logits`
+// holds this rank's n_local vocabulary columns (global columns col0 ...).
+// One CTA per row finds the shard's first maximum, stores (value, global
+// index) into slot m of every rank's exchange region for this call's epoch
+// (plane [parity][source rank]), raises its flag on every rank (lane p
+// release-stores to rank p, lane s acquire-polls rank s, bounded), then keeps
+// the first maximum over the ranks' candidates in rank order.  Shards are
+// ordered by rank, so this is the first maximum of the whole row: the index
+// torch.argmax returns.  Every rank computes the same ids.
+__global__ void __launch_bounds__(512) tp_argmax_kernel(const float* logits, int ld, int n_local,
+                                                        int col0, int* out, CommDev c) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
+  const int m = blockIdx.x;
+  const bool vec = (ld % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) % 16 == 0);
+  float bv;
+  int bi;
+  row_argmax(logits + (size_t)m * ld, n_local, vec, bv, bi);
+  const uint32_t epoch = c.state[0] * (uint32_t)c.n_sites + (uint32_t)c.site + 1u;
+  const int par = (int)(epoch & 1u);
+  const size_t plane = (size_t)((c.max_rows + 127) / 128) * 128 * (size_t)(c.n_cols + 256);
+  auto slot = [&](int p, int src) {
+    return reinterpret_cast<uint2*>(c.rs[p] + ((size_t)par * c.world + src) * plane) + m;
+  };
+  auto flag_at = [&](int p, int src) {
+    return c.flags[p] + ((size_t)(par * c.world + src)) * c.max_ctas + m;
+  };
+  if (threadIdx.x == 0) {
+    const uint2 cand = make_uint2(__float_as_uint(bv),
+                                  (uint32_t)(bi == 0x7fffffff ? bi : bi + col0));
+    for (int p = 0; p < c.world; ++p) *slot(p, c.rank) = cand;
+  }
+  __syncthreads();   // the candidate stores precede every lane's release
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32 && lane < c.world) {
+    st_release_sys(flag_at(lane, c.rank), epoch);
+    wait_flag_sys(flag_at(c.rank, lane), epoch);
+  }
+  __syncthreads();   // every rank's candidate visible to thread 0
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int s = 0; s < c.world; ++s) {
+      const uint2 cs = *slot(c.rank, s);
+      better(v, idx, __uint_as_float(cs.x), (int)cs.y);
+    }
+    out[m] = idx == 0x7fffffff ? 0 : idx;
+  }
+}
+
 }  // namespace tb
 
 using namespace tb;
@@ -135,6 +185,26 @@ int tb_comm_destroy(void* comm) {
   if (r && !rc) rc = r;
   delete c;
   return rc;
+}
+
+int tb_argmax_vocab_parallel(void* comm, const float* logits, int ld, int M, int n_local,
+                             int col0, int* out, int site, int n_sites, void* stream) {
+  CommHost* c = static_cast<CommHost*>(comm);
+  if (c == nullptr || c->dev.state == nullptr) {
+    set_last_error("communicator not opened");
+    return TB_ERR_STATE;
+  }
+  if (M < 0 || n_local < 0 || col0 < 0 || (n_local > 0 && ld < n_local) || out == nullptr)
+    return arg_err("argmax shapes");
+  if (M > c->max_rows || M > c->max_ctas)
+    return arg_err("argmax rows above the communicator's max_rows / max_ctas");
+  if (site < 0 || site >= n_sites) return arg_err("site must be in [0, n_sites)");
+  if (M == 0) return TB_OK;
+  CommDev d = c->dev;
+  d.site = site;
+  d.n_sites = n_sites;
+  return launch_pdl(tp_argmax_kernel, dim3(M), dim3(512), 0, static_cast<cudaStream_t>(stream), 1,
+                    "vocab-parallel argmax launch", logits, ld, n_local, col0, out, d);
 }
 
 int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int ldw, int M, int N,

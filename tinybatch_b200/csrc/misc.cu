@@ -48,16 +48,16 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
   }
 }
 
-// One CTA per row; ties go to the smallest index (torch.argmax semantics).
-__global__ void __launch_bounds__(512) argmax_kernel(const float* logits, int ld, int N, int* out) {
+// First maximum of row[0, N) over the calling CTA (blockDim.x a multiple of
+// 32, at most 512; every thread calls it).  Thread 0 returns the row's
+// largest value and its smallest index (torch.argmax semantics); the index
+// is 0x7fffffff when no element compares greater than -inf.  `vec`: the row
+// may be read as float4 (16-byte aligned row start).
+__device__ __forceinline__ void row_argmax(const float* row, int N, bool vec, float& bv, int& bi) {
   __shared__ float sv[16];
   __shared__ int si[16];
-  pdl_wait();
-  if (threadIdx.x == 0) pdl_trigger();
-  const float* row = logits + (size_t)blockIdx.x * ld;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  const bool vec = (ld % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) % 16 == 0);
+  bv = -INFINITY;
+  bi = 0x7fffffff;
   if (vec) {
     const int n4 = N / 4;
     const float4* r4 = reinterpret_cast<const float4*>(row);
@@ -104,8 +104,18 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* logits, int ld
     bv = sv[0];
     bi = si[0];
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
-    out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
   }
+}
+
+// One CTA per row; ties go to the smallest index (torch.argmax semantics).
+__global__ void __launch_bounds__(512) argmax_kernel(const float* logits, int ld, int N, int* out) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
+  const bool vec = (ld % 4 == 0) && (reinterpret_cast<uintptr_t>(logits) % 16 == 0);
+  float bv;
+  int bi;
+  row_argmax(logits + (size_t)blockIdx.x * ld, N, vec, bv, bi);
+  if (threadIdx.x == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
 }
 
 int embed_launch(const int* ids, int M, const void* emb, int ld_emb, int d, int vocab,

@@ -112,6 +112,15 @@ def plan_gemm(M: int, N: int, K: int, bns=(64, 128, 192, 256), max_splits: int =
     return best[1], best[2]
 
 
+def vocab_shard(vocab: int, rank: int, world: int) -> tuple[int, int]:
+    """(first column, columns) of a rank's slice of a vocabulary-parallel LM
+    head: ceil(vocab / world) columns per rank in rank order, the last slice
+    shorter (possibly empty)."""
+    per = -(-vocab // world)
+    col0 = min(rank * per, vocab)
+    return col0, max(0, min(per, vocab - col0))
+
+
 # Resident CTAs of the decode attention kernel on a B200 (148 SMs x 3).
 ATTN_SLOTS = 148 * 3
 ATTN_MAX_SPLIT = 8192
@@ -370,6 +379,14 @@ class DeviceModel:
         # epilogue (0: off; on the 14B decode step it lengthened the issuing
         # GEMM by more than it saved the next one)
         self.l2_prefetch_bytes = l2_prefetch_bytes
+        # with a communicator, sampled steps score only this rank's slice of
+        # the vocabulary and exchange argmax candidates (tb_argmax_vocab_parallel);
+        # full logits (sample=False) still come from the whole, replicated head
+        self.vocab_parallel = comm is not None
+        # exchange sites of one forward: o_proj and down_proj of every layer,
+        # then the sampling exchange (always counted, so every forward has the
+        # same epochs whether it samples or not)
+        self.n_sites = 2 * self.cfg.n_layers + 1
         # split-K scratch (arrival counters must stay zero between calls) and
         # split-KV attention scratch live in separate arenas
         self.scratch = ops.Scratch(self.device, 1 << 20)
@@ -438,7 +455,7 @@ class DeviceModel:
         else:
             self._run(f"{proj}_allreduce_residual", nbytes, 2.0 * T * Nn * K,
                       self.comm.row_linear_residual, x, wmat, self.h[:T], g_next, self.hg[:T],
-                      self.sq, site=site, n_sites=2 * self.cfg.n_layers, **kw)
+                      self.sq, site=site, n_sites=self.n_sites, **kw)
         return ops.row_parts(Nn, bn, splits)
 
     def plans(self, T: int, n: int) -> dict:
@@ -457,7 +474,12 @@ class DeviceModel:
                              paired=True)[1]),
             "down": plan_gemm(T, L.wd.shape[0], L.wd.shape[1]),
             "lm": plan_gemm(n, cfg.vocab_size, cfg.d_model),
+            "lm_shard": plan_gemm(n, max(1, vocab_shard(cfg.vocab_size, 0, self._world())[1]),
+                                  cfg.d_model),
         }
+
+    def _world(self) -> int:
+        return self.comm.world if self.comm is not None else 1
 
     def _next(self, w: torch.Tensor, plan) -> "N.L2Prefetch | None":
         return N.l2_next(w, plan[1], self.l2_prefetch_bytes)
@@ -535,9 +557,23 @@ class DeviceModel:
                               pl["down"], nxt)
         if not compute_logits:
             return None
+        V = cfg.vocab_size
+        if sample and self.comm is not None and self.vocab_parallel:
+            # each rank scores its vocabulary slice; the argmax exchanges one
+            # (value, index) candidate per row and rank
+            col0, nv = vocab_shard(V, self.comm.rank, self.comm.world)
+            out = self.logits[:n, :nv]
+            if nv:
+                bn, splits = pl["lm_shard"]
+                self._run("lm_head", 2 * nv * d + 2 * n * d + 4 * n * nv, 2.0 * n * nv * d,
+                          ops.linear, self.hg_last[:n], W.lm_head[col0:col0 + nv], out,
+                          sq=self.sq_last[:parts], inv_d=inv_d, eps=eps, bn=bn, splits=splits,
+                          scratch=self.scratch)
+            self._run("argmax", 4 * n * nv, 0.0, self.comm.argmax, self.logits[:n], nv, col0,
+                      self.next_ids[:n], site=2 * cfg.n_layers, n_sites=self.n_sites)
+            return out
         bn, splits = pl["lm"]
         out = self.logits[:n]
-        V = cfg.vocab_size
         self._run("lm_head", 2 * V * d + 2 * n * d + 4 * n * V, 2.0 * n * V * d, ops.linear,
                   self.hg_last[:n], W.lm_head, out, sq=self.sq_last[:parts], inv_d=inv_d,
                   eps=eps, bn=bn, splits=splits, scratch=self.scratch)
