@@ -187,6 +187,9 @@ class LLMEngine:
             return self._step_overlapped()
         if self._inflight is not None:
             return self.drain()
+        return self._step_plain(forced_tokens)
+
+    def _step_plain(self, forced_tokens: list[int] | None) -> list[StepOutput]:
         batch = self.scheduler.schedule()
         if batch.is_empty():
             return []
@@ -238,7 +241,7 @@ class LLMEngine:
     def _step_overlapped(self) -> list[StepOutput]:
         if self._inflight is None:
             if not self._overlap_ready(None):
-                return self._plain_step()
+                return self._step_plain(None)
             self._inflight = self._launch(None)
         nxt = self._launch(self._inflight) if self._overlap_ready(self._inflight) else None
         out = self._collect(self._inflight)
@@ -247,13 +250,6 @@ class LLMEngine:
             nxt = None
         self._inflight = nxt
         return out
-
-    def _plain_step(self) -> list[StepOutput]:
-        overlap, self.cfg.overlap_steps = self.cfg.overlap_steps, False
-        try:
-            return self.step()
-        finally:
-            self.cfg.overlap_steps = overlap
 
     def _overlap_ready(self, inflight: _InFlight | None) -> bool:
         """Whether the next step is a decode of exactly the running sequences
