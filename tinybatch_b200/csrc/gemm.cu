@@ -160,15 +160,6 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, f
                : "memory");
 }
 
-__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-
 // ------------------------------------------------------------- staging
 // A 16-column chunk of a 128-row tile in shared memory: [4 float4][BM rows],
 // chunks numbered [source][slot] (cluster split-K keeps one source per
