@@ -40,7 +40,7 @@ extern "C" {
 
 /* Device status codes (tb_status). */
 #define TB_STATUS_MBAR_TIMEOUT 101 /* a pipeline barrier wait ran out */
-#define TB_STATUS_PEER_TIMEOUT 102 /* a cross-GPU flag wait ran out */
+#define TB_STATUS_PEER_TIMEOUT 102 /* a wait for a peer GPU's data ran out */
 #define TB_STATUS_BAD_INDEX 103    /* block id / position / slot out of range */
 
 int tb_version(void);
@@ -49,7 +49,8 @@ const char* tb_last_error(void);
 /* Debug timeline: while buf is not NULL, every GEMM launched afterwards by
  * this process writes, per CTA c, %globaltimer stamps (ns) to buf[16*c + k]
  * for k = 0 start, 1 loads issued, 2 accumulator ready, 3 partials pushed
- * to the peer ranks, 4 partners seen, 5 sums delivered, 6 end, 7 split-K
+ * to the peer ranks, 4 owned sums sent (two-shot), 5 every value of the
+ * all-reduce received, 6 end, 7 split-K
  * chunks stored to their cluster owners, 8 every cluster member's chunks
  * arrived (unreached points are left as they were).  buf must hold 16 entries per CTA of the largest
  * launch.  Not thread-safe; NULL turns it off. */
@@ -86,20 +87,6 @@ int tb_status(unsigned int* code_h, int clear);
  */
 size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits);
 
-/* Optional L2 warm-up carried by a GEMM call for the weight the NEXT kernel
- * streams (decode steps are weight-bound; a GEMM's epilogue leaves HBM idle).
- * Once a CTA's main loop is done, the library issues L2 prefetches of the
- * first `bytes` of every (row, K segment) of the bf16 matrix [rows, k] with
- * row pitch ld elements, the K segments being the next call's split-K ranges
- * (splits of ceil(k/64) 64-column blocks).  A hint: results never depend on
- * it.  base 16-byte aligned, ld a multiple of 8, bytes a multiple of 16.
- * Pass NULL (or base == NULL) for none. */
-typedef struct tb_l2_prefetch {
-  const void* base;
-  long long ld;
-  int rows, k, splits, bytes;
-} tb_l2_prefetch;
-
 /* How many clusters of `cluster` GEMM CTAs (tile width bn) fit on the current
  * device at once (cudaOccupancyMaxActiveClusters); for choosing splits. */
 int tb_gemm_max_active_clusters(int bn, int cluster, int* out_h);
@@ -110,7 +97,7 @@ int tb_gemm_max_active_clusters(int bn, int cluster, int* out_h);
 int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
               const float* sq, int sq_parts, int sq_ld, float inv_d, float eps,
               void* out, int ld_out, int out_f32, int bn, int splits,
-              void* ws, size_t ws_bytes, const tb_l2_prefetch* next, void* stream);
+              void* ws, size_t ws_bytes, void* stream);
 
 /* Bytes of split-K scratch built into the library for
  * tb_linear_static_scratch: 4 KiB of arrival counters (at most 1024 output
@@ -125,12 +112,13 @@ int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int 
  * that scratch from a fixed array inside the library
  * (TB_STATIC_SCRATCH_BYTES per device, held by every GPU that loads the
  * library until the process exits) and allocates nothing.  Arguments and
- * result are those of tb_linear without ws/ws_bytes and next.
+ * result are those of tb_linear without ws/ws_bytes.
  *   - A call whose split-K scratch would exceed the array (or 1024 tiles)
  *     fails with TB_ERR_ARG and a message naming the size it needed.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture.
+ *     before any stream capture.  After a device reset (a new primary
+ *     context) the next call looks it up again.
  *   - All calls on a device share the array and it keeps the last call's
  *     contents; each call clears the counters it needs.  Calls that may run
  *     at the same time on one device (unordered streams) race on it. */
@@ -155,8 +143,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
                    const float* rope_cos, const float* rope_sin, int max_pos,
                    const int* positions, const int* slots,
                    void* q_out, int ld_q, void* kv_pool, int block_size,
-                   int bn, int splits, void* ws, size_t ws_bytes,
-                   const tb_l2_prefetch* next, void* stream);
+                   int bn, int splits, void* ws, size_t ws_bytes, void* stream);
 
 /* Column-parallel gate/up projection with SwiGLU epilogue.  w_gu holds, for
  * each output tile t of width bn, the bn/2 gate rows of features
@@ -167,7 +154,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
 int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, int K,
                       int n_feat, const float* sq, int sq_parts, int sq_ld, float inv_d,
                       float eps, void* act, int ld_act, int bn, int splits,
-                      void* ws, size_t ws_bytes, const tb_l2_prefetch* next, void* stream);
+                      void* ws, size_t ws_bytes, void* stream);
 
 /* Row-parallel projection + residual + next-norm prologue, single rank:
  *   h[m, :] += x . w^T  (fp32 residual stream, in place)
@@ -183,56 +170,69 @@ int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M
                            float* h, int ld_h, const void* g_next, void* hg, int ld_hg,
                            float* sq_out, int sq_out_ld, const int* row_dst, void* hg2,
                            float* sq2, int sq2_ld, int bn, int splits, void* ws,
-                           size_t ws_bytes, const tb_l2_prefetch* next, void* stream);
+                           size_t ws_bytes, void* stream);
 
 /* ------------------------------------------------- tensor-parallel comm
  * One communicator per rank (one process per GPU).  It owns one device
- * allocation per rank (exchange buffers for max_rows x n_cols bf16 partials,
- * delivery flags for max_ctas CTAs, a step counter), made at creation and
+ * allocation per rank (exchange buffers for max_rows x n_cols bf16 partials
+ * and sums, argmax candidate slots for max_rows rows), made at creation and
  * shared with the other ranks through CUDA IPC:
  *   1. tb_comm_create on every rank -> a 64-byte cudaIpcMemHandle;
  *   2. exchange the handles (e.g. torch.distributed all_gather);
  *   3. tb_comm_open with all world handles in rank order;
- *   4. per forward: tb_comm_begin_step, then the row-parallel projections
- *      with site = 0, 1, ... n_sites-1 in the same order on every rank;
+ *   4. the exchange calls below, the same calls in the same order on every
+ *      rank;
  *   5. after a barrier, tb_comm_destroy.
+ * The exchanges carry no flags: every buffer word holds an all-ones sentinel
+ * until a peer's data lands, the receiver polls the data itself and puts the
+ * sentinel back.  Each call names a sequence number `seq`; its parity picks
+ * one of two buffer halves.  Rules (the caller keeps them; a violation can
+ * mix two calls' data):
+ *   - consecutive tb_row_linear_allreduce_residual calls on a communicator
+ *     have seq of alternating parity (e.g. 2l and 2l+1 for layer l);
+ *   - consecutive tb_argmax_vocab_parallel calls alternate parity too, or
+ *     have at least one row-parallel call between them.
+ * A wait that runs out (5 s) sets TB_STATUS_PEER_TIMEOUT and leaves data in
+ * the buffers: destroy and recreate the communicator after one.
  * Replaces torch.distributed all_reduce(SUM) in the reference's
  * tensor_parallel.py:76-84 (called at :108 and :114). */
-int tb_comm_create(int rank, int world, int max_rows, int n_cols, int max_ctas, void** comm_out,
+int tb_comm_create(int rank, int world, int max_rows, int n_cols, void** comm_out,
                    void* ipc_handle_out);
 int tb_comm_open(void* comm, const void* ipc_handles);
-int tb_comm_begin_step(void* comm, void* stream);
 int tb_comm_destroy(void* comm);
 
 /* Row-parallel projection with the all-reduce fused into its epilogue:
  *   h += sum over ranks of (x_r . w_r^T)   (x_r, w_r: this rank's K shard)
  * then hg / sq_out as tb_row_linear_residual.  Each CTA pushes its bf16
- * partial tile to the peers over NVLink (two_shot = 0: to every rank, which
- * sums the partials in rank order; two_shot = 1: each row to the row's owner
- * rank, which sums and broadcasts), so h stays identical on all ranks.  Every rank must
- * make the same calls (same M, N, K, bn, splits, site) in the same order.
- * A partner that does not arrive within 5 s sets TB_STATUS_PEER_TIMEOUT.
+ * partial of every 16-column unit of its tile over NVLink: two_shot = 0 to
+ * every rank, which sums the world partials in rank order; two_shot = 1 to
+ * the unit's owner rank ((tile * bn/16 + unit) % world), which sums them in
+ * rank order and sends the bf16 sum to every rank.  Every rank adds the same
+ * values, so h stays identical on all ranks.  Every rank must make the same
+ * calls (same M, N, K, bn, splits, seq, two_shot) in the same order.
+ * span_ns (optional device pointer): the call raises *span_ns to the longest
+ * time, in ns, that any of its CTAs spent between starting to push and
+ * holding every sum it needs (the exchange's share of the call).
  * Replaces allreduce(F.linear(attn, Wo)) / allreduce(F.linear(act, Wd)) + the
- * residual add and next _rms_norm (tensor_parallel.py:108-110, :114-116). */
+ * residual add and next _rms_norm (tensor_parallel.py:76-84, :108-110, :114-116). */
 int tb_row_linear_allreduce_residual(const void* x, int ldx, const void* w, int ldw, int M, int N,
                                      int K, float* h, int ld_h, const void* g_next, void* hg,
                                      int ld_hg, float* sq_out, int sq_out_ld, const int* row_dst,
-                                     void* hg2, float* sq2, int sq2_ld, void* comm, int site,
-                                     int n_sites, int two_shot, int bn, int splits,
-                                     const tb_l2_prefetch* next, void* stream);
+                                     void* hg2, float* sq2, int sq2_ld, void* comm, int seq,
+                                     int two_shot, unsigned long long* span_ns, int bn,
+                                     int splits, void* stream);
 
 /* Greedy sampling over a vocabulary-parallel LM head: row m of logits
  * (fp32, row pitch ld) holds this rank's n_local vocabulary columns, global
  * columns col0 .. col0+n_local-1 (shards ordered by rank).  Every rank
  * writes out[m] = the first index of the row's maximum over the whole
  * vocabulary (torch.argmax of the full row; 0 when no value exceeds -inf).
- * The candidates travel through the communicator like a row-parallel call:
- * site is this call's place in the forward's n_sites, the same on every
- * rank.  M <= max_rows and M <= max_ctas.  Replaces the replicated
- * F.linear(h, lm_head) + argmax of the reference (tensor_parallel.py:117,
- * engine.py:149-151) for the sampled rows. */
+ * One (value, index) candidate per row and rank travels through the
+ * communicator (seq: see the rules above).  M <= max_rows.  Replaces the
+ * replicated F.linear(h, lm_head) + argmax of the reference
+ * (tensor_parallel.py:117, engine.py:149-151) for the sampled rows. */
 int tb_argmax_vocab_parallel(void* comm, const float* logits, int ld, int M, int n_local,
-                             int col0, int* out, int site, int n_sites, void* stream);
+                             int col0, int* out, int seq, void* stream);
 
 /* ------------------------------------------------------------- attention
  * Paged GQA attention reading K/V through block tables (no gather copy).

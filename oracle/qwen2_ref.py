@@ -61,7 +61,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> t
     return y
 
 
-def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, first_pos: int) -> torch.Tensor:
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, first_pos: int,
+              round_p: bool = False) -> torch.Tensor:
     """Causal GQA attention for one sequence.
 
     q ``[q_len, H, hd]``; k, v ``[ctx, KV, hd]``; query i (absolute position
@@ -69,7 +70,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, first_pos: int)
     kv head ``h // (H // KV)`` (``repeat_interleave`` in
     ``src/tinybatch/model.py:136-137``).  Scale ``1/sqrt(hd)``; the masks of
     ``src/tinybatch/model.py:139-146`` (``is_causal`` when q_len == ctx, else
-    ``mask[i, :first_pos+i+1]``) are both this rule."""
+    ``mask[i, :first_pos+i+1]``) are both this rule.
+
+    ``round_p`` models a kernel that multiplies bf16 probabilities with V:
+    ``exp(s - rowmax)`` is rounded to bf16 before the PV product while the
+    normaliser sums the unrounded values."""
     q, k, v = _f32(q), _f32(k), _f32(v)
     q_len, H, hd = q.shape
     ctx, KV, _ = k.shape
@@ -79,8 +84,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, first_pos: int)
     s = torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(hd)
     allowed = torch.arange(ctx)[None, :] <= (first_pos + torch.arange(q_len))[:, None]
     s = s.masked_fill(~allowed[None], float("-inf"))
-    p = torch.softmax(s, dim=-1)
-    return torch.einsum("hqk,khd->qhd", p, v)
+    if not round_p:
+        p = torch.softmax(s, dim=-1)
+        return torch.einsum("hqk,khd->qhd", p, v)
+    e = torch.exp(s - s.amax(dim=-1, keepdim=True))
+    return torch.einsum("hqk,khd->qhd", _bf16(e), v) / e.sum(dim=-1).transpose(0, 1)[..., None]
 
 
 # ----------------------------------------------------------------- paged KV
@@ -142,6 +150,31 @@ def _bf16(t: torch.Tensor) -> torch.Tensor:
     return t.to(torch.bfloat16).to(torch.float32)
 
 
+# Tensors a bf16-storage forward rounds, by name:
+#   gemm_in  the normed GEMM inputs bf16(h * g) of q/k/v and gate/up
+#   head_in  the normed input of the LM head
+#   q, kv    the rotated queries, and the keys/values stored in the pool
+#   p        attention probabilities entering the PV product
+#   attn     the attention output (o_proj input)
+#   act      the SwiGLU output (down_proj input)
+BF16_TENSORS = frozenset({"gemm_in", "head_in", "q", "kv", "p", "attn", "act"})
+# ``emulate_bf16=True``: the stored activations (every name but ``p``)
+BF16_STORED = frozenset(BF16_TENSORS - {"p"})
+
+
+def _emu_set(emulate) -> frozenset:
+    """``emulate_bf16`` argument -> set of tensor names to round."""
+    if emulate is True:
+        return BF16_STORED
+    if not emulate:
+        return frozenset()
+    names = frozenset(emulate)
+    unknown = names - BF16_TENSORS
+    if unknown:
+        raise ValueError(f"unknown bf16 tensors {sorted(unknown)}")
+    return names
+
+
 def _normed_linear(h, g, wt, b, eps, emulate):
     """``linear(rms_norm(h, g), wt, b)``.  With ``emulate`` the norm is
     applied the way the GPU path does it: the GEMM reads bf16(h * g) and its
@@ -156,44 +189,48 @@ def _normed_linear(h, g, wt, b, eps, emulate):
 
 
 def paged_layer(cfg, w, layer: int, h, positions, seq_slices, block_tables, context_lens,
-                pool, block_size: int, emulate_bf16: bool = False):
+                pool, block_size: int, emulate_bf16=False):
     """One decoder layer of ``Qwen2Paged.forward`` (``src/tinybatch/model.py:114-154``):
     norm -> q/k/v (+bias) -> RoPE -> KV scatter -> per-sequence attention over
     the paged context -> o_proj + residual -> norm -> SwiGLU MLP + residual.
 
-    ``emulate_bf16`` rounds to bf16 where the GPU path stores bf16 (GEMM
-    inputs, q, the KV pool, the attention output, the SwiGLU output) while
-    keeping every sum in fp32 -- a model of a correct bf16-storage forward
-    used to bound the kernels' own error."""
+    ``emulate_bf16`` rounds to bf16 where a bf16-storage GPU forward does
+    (``True``: every stored activation; or a set of ``BF16_TENSORS`` names)
+    while keeping every sum in fp32 -- a model of a correct bf16 forward used
+    to bound the kernels' own error and to attribute it to single tensors."""
+    emu = _emu_set(emulate_bf16)
     p = f"model.layers.{layer}."
     T = h.shape[0]
     g_in = w[p + "input_layernorm.weight"]
     n_heads, n_kv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    gin = "gemm_in" in emu
     q = _normed_linear(h, g_in, w[p + "self_attn.q_proj.weight"],
-                       w.get(p + "self_attn.q_proj.bias"), cfg.rms_eps, emulate_bf16)
+                       w.get(p + "self_attn.q_proj.bias"), cfg.rms_eps, gin)
     k = _normed_linear(h, g_in, w[p + "self_attn.k_proj.weight"],
-                       w.get(p + "self_attn.k_proj.bias"), cfg.rms_eps, emulate_bf16)
+                       w.get(p + "self_attn.k_proj.bias"), cfg.rms_eps, gin)
     v = _normed_linear(h, g_in, w[p + "self_attn.v_proj.weight"],
-                       w.get(p + "self_attn.v_proj.bias"), cfg.rms_eps, emulate_bf16)
+                       w.get(p + "self_attn.v_proj.bias"), cfg.rms_eps, gin)
     q = rope(q.view(T, n_heads, hd), positions, cfg.rope_theta)
     k = rope(k.view(T, n_kv, hd), positions, cfg.rope_theta)
     v = v.view(T, n_kv, hd)
-    if emulate_bf16:
-        q, k, v = _bf16(q), _bf16(k), _bf16(v)
+    if "q" in emu:
+        q = _bf16(q)
+    if "kv" in emu:
+        k, v = _bf16(k), _bf16(v)
     kv_write(pool, k, v, positions, seq_slices, block_tables, block_size)
     attn = torch.empty(T, n_heads * hd)
     for (s, e), table, ctx in zip(seq_slices, block_tables, context_lens):
         keys, vals = kv_gather(pool, table, ctx)
-        out = attention(q[s:e], keys, vals, first_pos=ctx - (e - s))
+        out = attention(q[s:e], keys, vals, first_pos=ctx - (e - s), round_p="p" in emu)
         attn[s:e] = out.reshape(e - s, -1)
-    if emulate_bf16:
+    if "attn" in emu:
         attn = _bf16(attn)
     h = h + linear(attn, w[p + "self_attn.o_proj.weight"])
     g_post = w[p + "post_attention_layernorm.weight"]
-    gate = _normed_linear(h, g_post, w[p + "mlp.gate_proj.weight"], None, cfg.rms_eps, emulate_bf16)
-    up = _normed_linear(h, g_post, w[p + "mlp.up_proj.weight"], None, cfg.rms_eps, emulate_bf16)
+    gate = _normed_linear(h, g_post, w[p + "mlp.gate_proj.weight"], None, cfg.rms_eps, gin)
+    up = _normed_linear(h, g_post, w[p + "mlp.up_proj.weight"], None, cfg.rms_eps, gin)
     act = torch.nn.functional.silu(gate) * up
-    if emulate_bf16:
+    if "act" in emu:
         act = _bf16(act)
     return h + linear(act, w[p + "mlp.down_proj.weight"])
 
@@ -212,7 +249,7 @@ def lm_head_weight(cfg, w):
 
 @torch.inference_mode()
 def paged_forward(cfg, w, token_ids, positions, seq_slices, block_tables, context_lens,
-                  pools, block_size: int, emulate_bf16: bool = False) -> torch.Tensor:
+                  pools, block_size: int, emulate_bf16=False) -> torch.Tensor:
     """``Qwen2Paged.forward`` (``src/tinybatch/model.py:100-158``): logits of the
     last token of every sequence, ``[n_seqs, vocab]`` fp32.  ``pools`` are
     updated in place, like the reference's ``PagedKVCache``.  See
@@ -224,7 +261,7 @@ def paged_forward(cfg, w, token_ids, positions, seq_slices, block_tables, contex
                         pools[layer], block_size, emulate_bf16)
     last = torch.tensor([e - 1 for _, e in seq_slices], dtype=torch.long)
     return _normed_linear(h[last], w["model.norm.weight"], lm_head_weight(cfg, w), None,
-                          cfg.rms_eps, emulate_bf16)
+                          cfg.rms_eps, "head_in" in _emu_set(emulate_bf16))
 
 
 def shard(w: dict, rank: int, world: int) -> dict:

@@ -25,6 +25,13 @@ Cases:
   qwen05b      config "qwen2.5-0.5b" (seed 1, bf16-valued weights): two
                prompts, paged prefill and one decode step; top-64 logits
                and a fixed index sample
+  tp_gate      a model whose heads, kv heads and d_ff divide 2, 4 and 8 (2
+               layers, d 1024, 16 q / 8 kv heads of 64, ff 2048, vocab 512,
+               bf16-valued weights seed 7), 40 ids (seed 7): tp_forward at
+               world 1 and run_tp_forward at world 2 -- the parity gate
+               bench.py runs before timing at every tensor-parallel degree
+
+``--update NAME ...`` recomputes only the named cases and keeps the others.
 """
 from __future__ import annotations
 
@@ -194,6 +201,8 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True)
     ap.add_argument("--skip-05b", action="store_true")
+    ap.add_argument("--update", nargs="*", default=None,
+                    help="recompute only these cases, keep the rest of golden.pt")
     args = ap.parse_args()
     sys.path.insert(0, args.reference_src)
     import tinybatch as _pkg  # noqa: F401
@@ -205,7 +214,33 @@ def main() -> None:
     import tinybatch.tensor_parallel
     ref = sys.modules["tinybatch"]
     torch.set_num_threads(8)
-    out: dict = {}
+    path = Path(__file__).parent / "golden.pt"
+    only = set(args.update) if args.update is not None else None
+    out: dict = torch.load(path, weights_only=False) if only is not None else {}
+
+    def want(name: str) -> bool:
+        return only is None or name in only
+
+    # ---- tp_gate
+    if want("tp_gate"):
+        from tinybatch_b200.config import ModelConfig
+        cfg = ModelConfig(n_layers=2, d_model=1024, n_heads=16, n_kv_heads=8, head_dim=64,
+                          d_ff=2048, vocab_size=512, rope_theta=1e6, rms_eps=1e-6,
+                          tie_embeddings=False, max_position=4096)
+        w = synthetic_weights(cfg, seed=7, dtype=torch.bfloat16)
+        w = {k: v.to(torch.float32) for k, v in w.items()}
+        ids = torch.randint(0, cfg.vocab_size, (40,), generator=torch.Generator().manual_seed(7))
+        rc = ref_cfg(ref, cfg)
+        l1 = ref.tensor_parallel.tp_forward(ids, w, rc, world=1)
+        l2, st2 = ref.tensor_parallel.run_tp_forward(2, w, rc, ids, port=29617)
+        out["tp_gate"] = dict(cfg={k: getattr(cfg, k) for k in cfg.__dataclass_fields__},
+                              seed=7, ids=ids.tolist(), fingerprint=fingerprint(w),
+                              logits_w1=l1, logits_w2=l2,
+                              stats_w2={k: st2[k] for k in ("calls", "bytes")})
+    if only is not None:
+        torch.save(out, path)
+        print(f"updated {sorted(only)} in {path} ({path.stat().st_size / 1024:.0f} KiB)")
+        return
 
     # ---- tiny_tp
     cfg = named_config("tiny")
@@ -288,7 +323,6 @@ def main() -> None:
                                   w["model.embed_tokens.weight"].double().abs().sum()),
                               **summ)
 
-    path = Path(__file__).parent / "golden.pt"
     torch.save(out, path)
     print(f"wrote {path} ({path.stat().st_size / 1024:.0f} KiB)")
 

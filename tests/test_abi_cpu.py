@@ -56,28 +56,25 @@ def test_host_only_entry_points(lib):
 
 @pytest.mark.parametrize("call,needle", [
     (lambda lib: lib.tb_linear(None, 0, None, 0, 128, 512, 512, None, 0, 0, 0.0, 0.0, None, 512,
-                               1, 100, 1, None, 0, None, None), "bn must be"),
+                               1, 100, 1, None, 0, None), "bn must be"),
     (lambda lib: lib.tb_qkv_rope_kv(None, 0, None, 0, None, 8, 256, 4, 2, 48, None, 0, 0, 0.0,
                                     0.0, None, None, 16, None, None, None, 0, None, 16, 128, 1,
-                                    None, 0, None, None), "multiple of head_dim"),
+                                    None, 0, None), "multiple of head_dim"),
     (lambda lib: lib.tb_gate_up_swiglu(None, 0, None, 0, 8, 256, 100, None, 0, 0, 0.0, 0.0,
-                                       None, 128, 128, 1, None, 0, None, None), "n_feat"),
+                                       None, 128, 128, 1, None, 0, None), "n_feat"),
     (lambda lib: lib.tb_paged_attention_decode(None, 0, None, 0, None, 1, 8, 2, 64, 16, None, 1,
                                                None, None, None, None, 1, 100, 500, None, 0,
                                                None), "split_tokens"),
-    (lambda lib: lib.tb_comm_begin_step(None, None), "communicator"),
-    (lambda lib: lib.tb_argmax_vocab_parallel(None, None, 512, 8, 256, 0, None, 96, 97, None),
+    (lambda lib: lib.tb_argmax_vocab_parallel(None, None, 512, 8, 256, 0, None, 3, None),
      "communicator"),
+    (lambda lib: lib.tb_row_linear_allreduce_residual(
+        None, 0, None, 0, 8, 512, 512, None, 0, None, None, 0, None, 0, None, None, None, 0,
+        None, 0, 0, None, 128, 1, None), "communicator"),
+    (lambda lib: lib.tb_linear_static_scratch(None, 0, None, 0, 128, 512, 512, None, 0, 0, 0.0,
+                                              0.0, None, 512, 1, 100, 1, None), "bn must be"),
 ])
 def test_argument_errors_are_reported(lib, call, needle):
     rc = call(lib)
     assert rc in (1, 4)          # TB_ERR_ARG / TB_ERR_STATE
     msg = lib.tb_last_error().decode()
     assert needle in msg, msg
-
-
-def test_l2_prefetch_struct_layout():
-    # tb_l2_prefetch {const void*; long long; int x4} as bound by ctypes
-    assert ctypes.sizeof(N.L2Prefetch) == 32
-    pf = N.L2Prefetch(0, 5120, 27648, 5120, 1, 4096)
-    assert (pf.rows, pf.k, pf.splits, pf.bytes) == (27648, 5120, 1, 4096)

@@ -144,3 +144,91 @@ def test_drain_returns_the_queued_step_once():
     eng._inflight = _inflight(reqs, _queue(reqs), [4])
     assert [o.token_id for o in eng.drain()] == [4]
     assert eng._inflight is None and eng.drain() == []
+
+
+class _Pools:
+    """Stand-in for the KV cache: one CPU pool per layer."""
+
+    def __init__(self, num_blocks, layers=2):
+        self.pools = [torch.zeros(num_blocks, 2, 1, 4, 2) for _ in range(layers)]
+
+
+def _spec_launch(eng):
+    """The host part of _launch: schedule the next decode step before the
+    previous step's tokens are known, build its batch, queue placeholders;
+    each sequence's KV slot of this step is marked in the pools."""
+    before = [(r, len(r.block_table)) for r in eng.scheduler.running]
+    batch = eng.scheduler.schedule()
+    assert not batch.prefill
+    eng.build_batch(batch)
+    for r in batch.decode:
+        pos = r.context_len() - 1
+        blk, off = r.block_table[pos // 4], pos % 4
+        for pool in eng.kv_cache.pools:
+            pool[blk, 0, 0, off, 0] = float(r.req_id)
+            pool[blk, 0, 0, off, 1] = float(pos)
+    slots = _queue(batch.decode)
+    return batch.decode, slots, before
+
+
+def _plain_run(prompts, max_new, stops, steps, num_blocks):
+    """Reference order: every step schedules, then applies its tokens and
+    frees what stopped.  Returns the (tables, free stack) after each step's
+    tokens are applied and the next step is scheduled."""
+    eng = _engine(num_blocks=num_blocks, stop=[9])
+    eng.cfg.overlap_steps = False
+    reqs = _running(eng, prompts, max_new)
+    states = []
+    batch = eng.scheduler.schedule()
+    eng.build_batch(batch)
+    for k in range(steps):
+        for i, r in enumerate(list(batch.decode)):
+            tok = 9 if (i, k) in stops else 1
+            r.output_token_ids.append(tok)
+            if tok == 9 or len(r.output_token_ids) >= r.max_new_tokens:
+                eng.scheduler.finish(r)
+        batch = eng.scheduler.schedule()
+        eng.build_batch(batch)
+        states.append(([list(r.block_table) for r in reqs], list(eng.block_manager.free_ids)))
+    return states
+
+
+def test_stop_token_keeps_the_reference_block_tables():
+    """A sequence stops on a stop token while the next step is already
+    queued, at steps where other sequences cross block boundaries: after the
+    queued step's reservations are redone, every table and the free stack
+    equal the plain engine's, and each continuing sequence's KV slot written
+    by the queued step sits in a block its table held before that step (the
+    redone reservations never move KV already written)."""
+    prompts = [[5] * 7, [6] * 3, [7] * 11, [8] * 2, [4] * 5]
+    max_new = [40] * 5
+    # (sequence index in the step's batch, step) that emits the stop token
+    stops = {(1, 1), (0, 4), (2, 9)}
+    steps = 12
+    want = _plain_run(prompts, max_new, stops, steps, num_blocks=40)
+
+    eng = _engine(num_blocks=40, stop=[9])
+    eng.kv_cache = _Pools(40)
+    reqs = _running(eng, prompts, max_new)
+    cur = _spec_launch(eng)
+    for k in range(steps):
+        nxt = _spec_launch(eng)        # queued before step k's tokens are read
+        toks = [9 if (i, k) in stops else 1 for i in range(len(cur[0]))]
+        f = _inflight(cur[0], cur[1], toks)
+        q = _InFlight(nxt[0], nxt[1], torch.zeros(len(nxt[0]), dtype=torch.int32), _Done(), 0,
+                      nxt[2])
+        eng._collect(f, q)
+        # the queued step's own sequences minus those that just stopped
+        cur = ([r for r in nxt[0] if r.status is Status.RUNNING],
+               [s for r, s in zip(nxt[0], nxt[1]) if r.status is Status.RUNNING])
+        tables = [list(r.block_table) for r in reqs]
+        assert (tables, list(eng.block_manager.free_ids)) == want[k], k
+        before = dict((id(r), n) for r, n in nxt[2])
+        for r in cur[0]:
+            assert r.output_token_ids[-1] == PENDING
+            pos = r.context_len() - 2          # the position the queued step wrote
+            assert pos // 4 < before[id(r)]
+            blk, off = r.block_table[pos // 4], pos % 4
+            for pool in eng.kv_cache.pools:
+                assert pool[blk, 0, 0, off, 0].item() == r.req_id
+                assert pool[blk, 0, 0, off, 1].item() == pos

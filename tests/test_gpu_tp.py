@@ -77,9 +77,8 @@ def _op_worker(rank, world, port, cases, queue):
             hg = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             parts = ops.row_parts(N, bn, splits)
             sq = torch.empty(parts, M, device=dev)
-            comm.begin_step()
             comm.row_linear_residual(xs[rank].to(dev), ws[rank].to(dev), h, gn.to(dev), hg, sq,
-                                     site=0, n_sites=1, bn=bn, splits=splits, two_shot=two_shot)
+                                     bn=bn, splits=splits, two_shot=two_shot)
             torch.cuda.synchronize()
             code = _native.status(clear=True)
             href, _ = R.row_gemm_allreduce_norm(xs, [w.t() for w in ws], h0, gn, 1e-6)
@@ -236,3 +235,82 @@ def test_vocab_parallel_sampling(world, tie):
         decisive = (top2[:, 0] - top2[:, 1]) > 1e-3
         assert int(decisive.sum()) >= 20
         assert torch.equal(ids0[decisive], ref[decisive])
+
+
+def _mixed_worker(rank, world, port, cfg, w, queue):
+    """Back-to-back forwards on one communicator, some sampling on the device
+    (row-parallel exchanges plus an argmax exchange) and some returning full
+    logits (row-parallel exchanges only), in an order that reuses every
+    buffer half many times; then tp_forward's exchange timing."""
+    import datetime
+    import random
+
+    import torch.distributed as dist
+
+    from tinybatch_b200 import _native
+    from tinybatch_b200.comm import TPComm
+    from tinybatch_b200.model import Qwen2Paged
+    from tinybatch_b200.tensor_parallel import shard_weights, tp_forward
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    comm = TPComm(rank, world, dev, cfg.d_model, max_rows=256)
+    try:
+        model = Qwen2Paged.from_weights(cfg, w, device=dev, rank=rank, world=world, comm=comm,
+                                        max_tokens=64, max_seqs=64)
+        rng = random.Random(4)
+        ctx = [rng.randint(1, 100) for _ in range(16)]
+        tables, nb = [], 0
+        for c in ctx:
+            k = -(-c // 16)
+            tables.append(list(range(nb, nb + k)))
+            nb += k
+        cache = model.make_kv_cache(nb, 16)
+        g = torch.Generator(device=dev).manual_seed(6)
+        for pool in cache.pools:
+            pool.copy_(torch.randn(pool.shape, generator=g, device=dev).mul_(0.5))
+        ids = [rng.randrange(cfg.vocab_size) for _ in ctx]
+        md = model.metadata(ids, [c - 1 for c in ctx], [(i, i + 1) for i in range(16)], tables,
+                            ctx, 16)
+        logits, sampled = [], []
+        for sample in (False, False, True, False, True, True, False, True, False, False):
+            out = model.dm.forward(md, cache.pools, sample=sample)
+            if sample:
+                sampled.append(model.dm.next_ids[:16].clone())
+            else:
+                logits.append(out.clone())
+        torch.cuda.synchronize()
+        _native.raise_on_status(f"rank {rank}")
+        same_logits = all(torch.equal(x, logits[0]) for x in logits)
+        same_ids = all(torch.equal(x, sampled[0]) for x in sampled)
+        stats = {"calls": 0, "bytes": 0, "seconds": 0.0}
+        shard = shard_weights(w, cfg, rank, world)
+        ids_t = torch.randint(0, cfg.vocab_size, (24,), generator=torch.Generator().manual_seed(1))
+        tp_forward(ids_t, shard, cfg, world, stats)
+        torch.cuda.synchronize()
+        _native.raise_on_status(f"rank {rank} tp_forward")
+        queue.put((rank, (same_logits, same_ids, logits[0].argmax(-1).cpu(), sampled[0].cpu(),
+                          stats)))
+    finally:
+        from tinybatch_b200.comm import close_all
+        close_all()
+        dist.destroy_process_group()
+
+
+def test_mixed_sampled_and_full_forwards_world2():
+    """Forwards with and without device sampling, back to back, on one
+    communicator: every repeat of the same step gives the same logits and the
+    same ids on every rank, no wait runs out, and tp_forward reports the
+    exchanges' device time in comm_stats["seconds"]."""
+    cfg = _small_tp_config()
+    w = synthetic_weights(cfg, 9, dtype=torch.bfloat16)
+    res = _spawn(2, _mixed_worker, (cfg, w), port=PORT + 90, timeout_s=300, collect_all=True)
+    for same_logits, same_ids, full_arg, ids, stats in res:
+        assert same_logits and same_ids
+        assert stats["calls"] == 2 * cfg.n_layers
+        assert 0.0 < stats["seconds"] < 1.0, stats
+    assert torch.equal(res[0][3], res[1][3])
+    assert torch.equal(res[0][2], res[1][2])

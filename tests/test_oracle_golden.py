@@ -42,6 +42,26 @@ def test_tp_forward_matches_reference(golden, name):
     assert case["stats_w2"]["bytes"] == 2 * cfg.n_layers * len(case["ids"]) * cfg.d_model * 4
 
 
+def test_tp_gate_case_matches_reference(golden):
+    """The parity-gate model bench.py checks at every tensor-parallel degree:
+    the oracle, emulating 1, 2, 4 and 8 ranks, reproduces the reference's
+    logits for the bf16-valued draw it recorded."""
+    from tinybatch_b200.config import ModelConfig
+    case = golden["tp_gate"]
+    cfg = ModelConfig(**case["cfg"])
+    w = {k: v.float() for k, v in synthetic_weights(cfg, case["seed"], dtype=torch.bfloat16).items()}
+    fp = fingerprint(w)
+    for k, v in case["fingerprint"].items():
+        assert fp[k] == pytest.approx(v, rel=1e-12), k
+    ids = torch.tensor(case["ids"])
+    for world in (1, 2, 4, 8):
+        torch.testing.assert_close(R.tp_forward(cfg, w, ids, world=world), case["logits_w1"],
+                                   atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(case["logits_w2"], case["logits_w1"], atol=1e-5, rtol=1e-5)
+    assert case["stats_w2"] == {"calls": 2 * cfg.n_layers,
+                                "bytes": 2 * cfg.n_layers * len(case["ids"]) * cfg.d_model * 4}
+
+
 def test_paged_prefill_matches_reference(golden):
     case = golden["tiny_tp"]
     cfg, w = _weights(case)

@@ -101,3 +101,46 @@ def test_silent_rank_times_out():
     with pytest.raises(RuntimeError, match="no result"):
         _spawn(2, _silent_worker, (), port=PORT + 3, timeout_s=3)
     assert time.time() - t0 < 20
+
+
+def test_exchange_sequence_parity_rules():
+    """Consecutive exchanges of one kind must alternate buffer halves: an
+    explicit seq with the previous call's parity is refused, an implicit one
+    takes the other half."""
+    from tinybatch_b200.comm import TPComm
+    assert TPComm._next(None, 1, "x") == 0
+    assert TPComm._next(None, 0, "x") == 1
+    assert TPComm._next(0, 1, "x") == 0
+    assert TPComm._next(7, 0, "x") == 7
+    with pytest.raises(ValueError):
+        TPComm._next(2, 0, "x")
+    with pytest.raises(ValueError):
+        TPComm._next(-1, 0, "x")
+    # a forward's row-parallel sites 0 .. 2L-1 start at parity 0 and end at 1,
+    # so back-to-back forwards (sampled or not) keep alternating
+    last = 1
+    for _ in range(3):
+        for site in range(2 * 4):
+            last = TPComm._next(site, last, "forward") & 1
+
+
+def _cpu_leg_worker(rank, world, port, queue):
+    """bench.py's CPU baseline at TP=2: each rank times its shard of a decoder
+    layer with gloo all-reduces; the reported times are the max over ranks."""
+    import bench
+    _init(rank, world, port)
+    try:
+        cfg = named_config("tiny")
+        info = bench.cpu_decode_sample(cfg, [5, 17, 33, 64], rank, world, dist.group.WORLD)
+        queue.put((rank, info))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_cpu_leg_tp2():
+    res = _spawn(2, _cpu_leg_worker, (), port=PORT + 40, timeout_s=120, collect_all=True)
+    a, b = res
+    assert a["layer_s"] == b["layer_s"] and a["lm_head_s"] == b["lm_head_s"]
+    cfg = named_config("tiny")
+    assert a["step_s"] == pytest.approx(cfg.n_layers * a["layer_s"] + a["lm_head_s"])
+    assert a["tokens_per_s"] == pytest.approx(4 / a["step_s"])

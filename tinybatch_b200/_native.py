@@ -17,7 +17,7 @@ _LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtinybatch_b200.so"
 _lib = None
 
 TB_OK = 0
-STATUS_NAMES = {101: "pipeline barrier wait ran out", 102: "peer flag wait ran out",
+STATUS_NAMES = {101: "pipeline barrier wait ran out", 102: "wait for a peer GPU's data ran out",
                 103: "block id / position / slot out of range"}
 
 _SIGS = {
@@ -29,8 +29,7 @@ _SIGS = {
     "tb_gemm_max_active_clusters": (c_int, [c_int, c_int, ctypes.POINTER(c_int)]),
     "tb_linear": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                           c_void_p, c_int, c_int, c_float, c_float,
-                          c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p,
-                          c_void_p]),
+                          c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "tb_linear_static_scratch": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                                          c_void_p, c_int, c_int, c_float, c_float,
                                          c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
@@ -38,15 +37,14 @@ _SIGS = {
                                c_int, c_int, c_int, c_void_p, c_int, c_int, c_float, c_float,
                                c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                c_void_p, c_int, c_void_p, c_int, c_int, c_int,
-                               c_void_p, c_size_t, c_void_p, c_void_p]),
+                               c_void_p, c_size_t, c_void_p]),
     "tb_gate_up_swiglu": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                                   c_void_p, c_int, c_int, c_float, c_float,
-                                  c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p,
-                                  c_void_p]),
+                                  c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "tb_row_linear_residual": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                                        c_void_p, c_int, c_void_p, c_void_p, c_int,
                                        c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int,
-                                       c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
+                                       c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "tb_attention_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "tb_paged_attention_decode": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
                                           c_int, c_int, c_int, c_int, c_void_p, c_int,
@@ -56,49 +54,24 @@ _SIGS = {
                                            c_int, c_int, c_int, c_int, c_void_p, c_int,
                                            c_void_p, c_void_p, c_void_p, c_int,
                                            c_void_p, c_int, c_void_p]),
-    "tb_comm_create": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p),
-                               c_void_p]),
+    "tb_comm_create": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p), c_void_p]),
     "tb_comm_open": (c_int, [c_void_p, c_void_p]),
-    "tb_comm_begin_step": (c_int, [c_void_p, c_void_p]),
     "tb_comm_destroy": (c_int, [c_void_p]),
     "tb_row_linear_allreduce_residual": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int,
                                                  c_int, c_void_p, c_int, c_void_p, c_void_p, c_int,
                                                  c_void_p, c_int, c_void_p, c_void_p, c_void_p,
-                                                 c_int, c_void_p, c_int, c_int, c_int, c_int,
-                                                 c_int, c_void_p, c_void_p]),
+                                                 c_int, c_void_p, c_int, c_int, c_void_p, c_int,
+                                                 c_int, c_void_p]),
     "tb_embed": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p,
                          c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "tb_argmax": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "tb_argmax_vocab_parallel": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
-                                         c_void_p, c_int, c_int, c_void_p]),
+                                         c_void_p, c_int, c_void_p]),
 }
 
 
 class NativeError(RuntimeError):
     pass
-
-
-class L2Prefetch(ctypes.Structure):
-    """``tb_l2_prefetch``: L2 warm-up request for the next kernel's weight."""
-    _fields_ = [("base", c_void_p), ("ld", ctypes.c_longlong), ("rows", c_int), ("k", c_int),
-                ("splits", c_int), ("bytes", c_int)]
-
-
-def l2_next(w: torch.Tensor | None, splits: int = 1, budget: int = 0) -> L2Prefetch | None:
-    """Request to warm L2 with ``budget`` bytes of weight ``w`` [rows, k]
-    (bf16, F.linear layout) as a GEMM with ``splits`` K segments will read
-    it: the same prefix of every (row, segment).  None when nothing fits."""
-    if w is None or budget <= 0:
-        return None
-    rows, k = w.shape
-    per = min(budget // (rows * max(splits, 1)), 2 * k, (1 << 30)) // 16 * 16
-    if per <= 0:
-        return None
-    return L2Prefetch(w.data_ptr(), w.stride(0), rows, k, max(splits, 1), per)
-
-
-def pf_arg(pf: L2Prefetch | None):
-    return ctypes.byref(pf) if pf is not None else None
 
 
 def lib_path() -> Path:

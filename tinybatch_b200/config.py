@@ -95,9 +95,9 @@ class EngineConfig:
     top_p: float = 1.0
     stop_token_ids: tuple = field(default_factory=tuple)
 
-    # engine: in a steady greedy decode batch, queue step k+1 on the device
-    # before reading step k's tokens back (``LLMEngine.step``); outputs are
-    # identical, block tables are not compared with the reference's in this mode
+    # engine: in a steady greedy decode batch (prefix caching off), queue step
+    # k+1 on the device before reading step k's tokens back
+    # (``LLMEngine.step``); tokens and block tables are those of the plain loop
     overlap_steps: bool = False
 
     def kv_pool_tokens(self) -> int:

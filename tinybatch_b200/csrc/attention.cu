@@ -600,17 +600,10 @@ static int decode_tma_launch(const AttnArgs& a, cudaStream_t st) {
   const int ring = TMA_STAGES * SLOT + 2 * TMA_STAGES * 8 + TMA_MAX_SPLIT_CHUNKS * 4;
   const int smem = (ring > merge ? ring : merge) + 1024;
   if (a.split_chunks > TMA_MAX_SPLIT_CHUNKS) return arg_err("split_tokens above 8192");
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_tma_kernel<HD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_decode_tma_kernel<HD>,
-                               cudaFuncAttributePreferredSharedMemoryCarveout,
-                               cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return host_err(e, "attention smem attribute");
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr_devs{0};
+  if (int rc = smem_attr_once(attn_decode_tma_kernel<HD>, smem, attr_devs,
+                              "attention smem attribute", true))
+    return rc;
   CUtensorMap map;
   const uint64_t rows = (uint64_t)a.num_blocks * 2 * a.n_kv_heads * a.block_size;
   int rc = make_tmap_2d(&map, a.pool, HD, rows, (uint64_t)HD * 2, 64, 16);
@@ -624,13 +617,9 @@ static int decode_launch(const AttnArgs& a, cudaStream_t st) {
   const int smem_ring = 4 * DEC_STAGES * 2 * ChunkLayout<HD>::BYTES;
   const int smem_merge = (4 * 16 * (HD + 4) + 2 * 4 * 16) * 4 + 16;
   const int smem = smem_ring > smem_merge ? smem_ring : smem_merge;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return host_err(e, "attention smem attribute");
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr_devs{0};
+  if (int rc = smem_attr_once(attn_decode_kernel<HD>, smem, attr_devs, "attention smem attribute"))
+    return rc;
   return launch_pdl(attn_decode_kernel<HD>, dim3(a.max_splits, a.n_kv_heads, a.n_seqs),
                     dim3(128), smem, st, 1, "attention decode launch", a);
 }

@@ -101,7 +101,7 @@ size_t tb_gemm_scratch_bytes(int M, int N, int bn, int splits) {
 int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
               const float* sq, int sq_parts, int sq_ld, float inv_d, float eps, void* out,
               int ld_out, int out_f32, int bn, int splits, void* ws, size_t ws_bytes,
-              const tb_l2_prefetch* next, void* stream) {
+              void* stream) {
   if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (out == nullptr || ld_out < N || (out_f32 ? ld_out % 4 : ld_out % 8))
     return arg_err("out / ld_out");
@@ -109,7 +109,6 @@ int tb_linear(const void* x, int ldx, const void* w, int ldw, int M, int N, int 
   g.out = out;
   g.ld_out = ld_out;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
-  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(out_f32 ? EPI_F32 : EPI_BF16, bn, x, ldx, w, ldw, g,
                      static_cast<cudaStream_t>(stream));
@@ -120,7 +119,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
                    int sq_parts, int sq_ld, float inv_d, float eps, const float* rope_cos,
                    const float* rope_sin, int max_pos, const int* positions, const int* slots,
                    void* q_out, int ld_q, void* kv_pool, int block_size, int bn, int splits,
-                   void* ws, size_t ws_bytes, const tb_l2_prefetch* next, void* stream) {
+                   void* ws, size_t ws_bytes, void* stream) {
   if (!valid_bn(bn) || head_dim <= 0 || head_dim % 16 || bn % head_dim)
     return arg_err("bn must be 64/128/192/256 and a multiple of head_dim (multiple of 16)");
   if (bias == nullptr || rope_cos == nullptr || rope_sin == nullptr || positions == nullptr ||
@@ -146,7 +145,6 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
   g.block_size = block_size;
   g.max_pos = max_pos;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
-  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(EPI_QKV, bn, x, ldx, w_qkv, ldw, g, static_cast<cudaStream_t>(stream));
 }
@@ -154,7 +152,7 @@ int tb_qkv_rope_kv(const void* x, int ldx, const void* w_qkv, int ldw, const voi
 int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, int K,
                       int n_feat, const float* sq, int sq_parts, int sq_ld, float inv_d,
                       float eps, void* act, int ld_act, int bn, int splits, void* ws,
-                      size_t ws_bytes, const tb_l2_prefetch* next, void* stream) {
+                      size_t ws_bytes, void* stream) {
   if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (n_feat <= 0 || n_feat % 16 || ld_act < n_feat || ld_act % 8 || act == nullptr)
     return arg_err("n_feat must be a multiple of 16; act / ld_act");
@@ -165,7 +163,6 @@ int tb_gate_up_swiglu(const void* x, int ldx, const void* w_gu, int ldw, int M, 
   g.ld_out = ld_act;
   g.n_feat = n_feat;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
-  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(EPI_SWIGLU, bn, x, ldx, w_gu, ldw, g, static_cast<cudaStream_t>(stream));
 }
@@ -174,7 +171,7 @@ int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M
                            float* h, int ld_h, const void* g_next, void* hg, int ld_hg,
                            float* sq_out, int sq_out_ld, const int* row_dst, void* hg2,
                            float* sq2, int sq2_ld, int bn, int splits, void* ws,
-                           size_t ws_bytes, const tb_l2_prefetch* next, void* stream) {
+                           size_t ws_bytes, void* stream) {
   if (!valid_bn(bn)) return arg_err("bn must be 64, 128, 192 or 256");
   if (N % 16 || h == nullptr || g_next == nullptr || hg == nullptr || sq_out == nullptr)
     return arg_err("N must be a multiple of 16; h / g_next / hg / sq_out");
@@ -194,7 +191,6 @@ int tb_row_linear_residual(const void* x, int ldx, const void* w, int ldw, int M
   g.sq2 = sq2;
   g.sq2_ld = sq2_ld;
   int rc = gemm_scratch(g, bn, ws, ws_bytes);
-  if (!rc) rc = gemm_set_prefetch(g, next);
   if (rc) return rc;
   return gemm_launch(EPI_RESID, bn, x, ldx, w, ldw, g, static_cast<cudaStream_t>(stream));
 }

@@ -113,35 +113,60 @@ __device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* smem_raw) {
   return smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 }
 
-// ------------------------------------------------------ cross-GPU signalling
+// ------------------------------------------------------ cross-GPU packets
+//
+// Cross-GPU exchanges carry no flags.  Every exchange word starts as the
+// all-ones sentinel; a sender stores its data with 8-byte-atomic (volatile,
+// system-coherent) stores straight into the receiver's buffer, and the
+// receiver polls the data words themselves until none is the sentinel, then
+// writes the sentinel back.  Data never equals the sentinel: packed bf16
+// words that would (four all-ones NaNs) are sent as four canonical NaNs.
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+constexpr unsigned long long TB_SENTINEL = ~0ull;
 
 // Peer waits get a longer budget than pipeline waits: ranks may drift apart
 // by host-side work between steps.
 constexpr uint64_t PEER_BUDGET_NS = 5000000000ull;
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ unsigned long long not_sentinel(unsigned long long x) {
+  return x == TB_SENTINEL ? 0x7FFF7FFF7FFF7FFFull : x;
 }
 
-// Bounded wait until *p == v, written by another GPU with a release store.
-// Polls with acquire loads (measured on B200 over NVLink: a release store
-// and acquire polling cost about what relaxed accesses do, while a system
-// fence adds ~1.5 us per side, more when many CTAs fence at once).
-__device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t v) {
-  if (ld_acquire_sys(p) != v) {
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1; ld_acquire_sys(p) != v; ++i) {
-      if ((i & 1023u) == 0 && globaltimer_ns() - t0 > PEER_BUDGET_NS) {
+// 16 bytes as two 8-byte words (each single-copy atomic).
+__device__ __forceinline__ void st_pkt(void* p, unsigned long long a, unsigned long long b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ void ld_pkt(const void* p, unsigned long long& a,
+                                       unsigned long long& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ void st_word(void* p, unsigned long long a) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_word(const void* p) {
+  unsigned long long a;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+
+// Bounded poll of one 16-byte packet: returns once neither word is the
+// sentinel (false, with ERR_PEER_TIMEOUT recorded, when the budget runs out).
+// t0: the caller's start time of this wait (0 = not started yet).
+__device__ __forceinline__ bool poll_pkt(const void* p, unsigned long long& a,
+                                         unsigned long long& b, uint64_t& t0) {
+  for (uint32_t i = 0; a == TB_SENTINEL || b == TB_SENTINEL; ++i) {
+    if ((i & 255u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > PEER_BUDGET_NS) {
         set_status(ERR_PEER_TIMEOUT);
         return false;
       }
     }
+    ld_pkt(p, a, b);
   }
   return true;
 }

@@ -65,40 +65,6 @@ __device__ __forceinline__ float row_scale(const GemmArgs& g, int m) {
   return rsqrtf(s * g.inv_d + g.eps);
 }
 
-// Warm L2 with this CTA's share of a weight the next kernel streams: for
-// every (256-row block, split segment) of pf, the first pf.bytes of the
-// segment's columns, as 256 x 256 tensor boxes (128 KiB per prefetch), items
-// spread over the grid and the warp's lanes.
-__device__ __forceinline__ void prefetch_box(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
-constexpr int PF_BOX = 256;
-
-__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, const CUtensorMap* map,
-                                                  int lane) {
-  const int num_k = (pf.k + BK - 1) / BK;
-  const int row_blocks = (pf.rows + PF_BOX - 1) / PF_BOX;
-  const int cols = pf.bytes / 2;
-  const int boxes = (cols + PF_BOX - 1) / PF_BOX;   // per (row block, segment)
-  const long long items = (long long)row_blocks * pf.splits * boxes;
-  const long long cta = blockIdx.x + (long long)blockIdx.y * gridDim.x;
-  const long long stride = (long long)gridDim.x * gridDim.y * 32;
-  for (long long it = cta * 32 + lane; it < items; it += stride) {
-    const int b = (int)(it % boxes);
-    const int z = (int)((it / boxes) % pf.splits);
-    const int rb = (int)(it / ((long long)boxes * pf.splits));
-    const int kb = (int)((long long)z * num_k / pf.splits);
-    const int ke = (int)((long long)(z + 1) * num_k / pf.splits);
-    const int x = kb * BK + b * PF_BOX;   // a multiple of 64 columns: 16-byte aligned
-    if (x >= min(ke * BK, pf.k)) continue;
-    prefetch_box(map, x, rb * PF_BOX);
-  }
-}
-
 // How a tile's columns are grouped for the epilogue and, in cluster split-K,
 // which member owns them.  The unit of work is a "pair" of cp 16-column
 // chunks that one thread finishes together: a single chunk (plain outputs,
@@ -344,96 +310,107 @@ __device__ __forceinline__ void for_resid_units(const GemmArgs& g, int m, int tn
   }
 }
 
-// 8 bf16 values as fp32, read around L1 (they were written by other GPUs).
-__device__ __forceinline__ void ld_bf16x8_cg(const __nv_bfloat16* p, float* v) {
-  const uint4 a = __ldcg(reinterpret_cast<const uint4*>(p));
-  const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+// 16 fp32 values as two 16-byte packets of bf16 (words w[0..3]; never the
+// sentinel).
+__device__ __forceinline__ void pack_pkts(const float* v, unsigned long long* w) {
+  uint32_t b[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = not_sentinel((unsigned long long)b[2 * i] | ((unsigned long long)b[2 * i + 1] << 32));
+}
+
+// v[0..15] += the 16 bf16 values of packets w[0..3].
+__device__ __forceinline__ void add_pkts(const unsigned long long* w, float* v) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float2 x = __bfloat1622float2(pa[i]);
-    v[2 * i] = x.x;
-    v[2 * i + 1] = x.y;
+    const uint32_t lo = (uint32_t)w[i], hi = (uint32_t)(w[i] >> 32);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&lo));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hi));
+    v[4 * i] += a.x;
+    v[4 * i + 1] += a.y;
+    v[4 * i + 2] += b.x;
+    v[4 * i + 3] += b.y;
   }
-}
-
-__device__ __forceinline__ void pack_bf16x16(const float* v, uint4& lo, uint4& hi) {
-  lo.x = pack_bf16x2(v[0], v[1]);
-  lo.y = pack_bf16x2(v[2], v[3]);
-  lo.z = pack_bf16x2(v[4], v[5]);
-  lo.w = pack_bf16x2(v[6], v[7]);
-  hi.x = pack_bf16x2(v[8], v[9]);
-  hi.y = pack_bf16x2(v[10], v[11]);
-  hi.z = pack_bf16x2(v[12], v[13]);
-  hi.w = pack_bf16x2(v[14], v[15]);
-}
-
-// Flag handshake of one exchange round, run by the first epilogue warp: lane
-// p release-stores this CTA's flag into rank p, then lane s waits (acquire
-// loads, bounded) for rank s's flag.  The lanes work in parallel: a release
-// store waits for everything ordered before it, so one thread storing every
-// rank's flag in turn pays one NVLink round trip per rank.  The caller's CTA
-// barrier before puts every epilogue thread's pushes before each lane's
-// release (release is cumulative); its CTA barrier after makes the acquired
-// data visible to every thread.
-template <class FS, class FR>
-__device__ __forceinline__ void exchange_flags(const CommDev& c, FS send_flag, FR recv_flag,
-                                               uint32_t epoch) {
-  const int lane = threadIdx.x & 31;
-  if (lane < c.world) {
-    st_release_sys(send_flag(lane), epoch);
-    wait_flag_sys(recv_flag(lane), epoch);
-  }
-  __syncwarp();
 }
 
 // Row-parallel epilogue with the all-reduce across tensor-parallel ranks
-// fused in (all 128 epilogue threads call it; it synchronises them).
+// fused in (the 128 epilogue threads, one output row each).
 //
-//   one-shot  every rank pushes its bf16 partial of the CTA's columns to
-//             every rank; each rank sums the world partials in rank order
-//   two-shot  every rank pushes each row's partial to the row's owner (rank
-//             row_in_tile * world / 128, so every CTA owns an equal share of
-//             its tile); the owner sums them in rank order and pushes the
-//             bf16 sum to every rank
+//   one-shot  every rank pushes its bf16 partial of each 16-column unit of
+//             the CTA's columns to every rank; each rank sums the world
+//             partials in rank order
+//   two-shot  unit u of tile t is owned by rank (t * BN/16 + u) % world:
+//             every rank pushes its partial of the unit to the owner only;
+//             the owner sums them in rank order and pushes the bf16 sum to
+//             every rank
 // Every rank then adds the same bf16 values to its replicated fp32 residual,
-// so h stays bit-identical on all ranks.  A CTA's partners are the CTAs
-// with the same index on the other ranks; "delivered" flags carry the call's
-// epoch (release stores by parallel lanes; acquire loads, bounded waits).
+// so h stays bit-identical on all ranks.  A CTA's partners are the CTAs with
+// the same tile and split on the other ranks.
+//
+// No flags: the exchange buffers hold the sentinel until the data lands
+// (8-byte-atomic packet stores over NVLink); each receiving thread polls its
+// own packets, sums them, and writes the sentinel back.  One NVLink
+// traversal per phase, no round trip for a release or a flag.
 //
 // Exchange layout: [tile][16-column unit][half][128 rows][8 columns] bf16, the
 // epilogue's own thread order (thread = row), so one warp store or load
-// instruction moves 512 contiguous bytes over NVLink.
+// instruction moves 512 contiguous bytes.
 template <int BN>
 __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader<BN>& acc, int tm,
-                                           int tn, int row, int own, int n_own,
-                                           const ResidPre& pre, int flag_slot,
-                                           uint64_t* acc_free) {
+                                              int tn, int row, int own, int n_own,
+                                              const ResidPre& pre, uint64_t* acc_free) {
   const CommDev& c = g.comm;
   const int m = tm * BM + row;
   const bool valid = m < g.M;
-  const int N = g.N;
-  const uint32_t epoch = c.state[0] * (uint32_t)c.n_sites + (uint32_t)c.site + 1u;
-  const int par = (int)(epoch & 1u);
+  const int N = g.N, W = c.world;
   // plane: every tile of a max_rows x n_cols output, padded to whole tiles
   const size_t plane = (size_t)((c.max_rows + BM - 1) / BM) * BM * (size_t)(c.n_cols + 256);
-  const int cta = flag_slot;   // this CTA's (tile's) flags: same index on every rank
-  const int row_owner = row * c.world / BM;   // two-shot: the rank that reduces this row
   const bool leader = threadIdx.x == 64;
-  const bool flag_warp = (threadIdx.x >> 5) == 2;   // the first epilogue warp
   constexpr int U = BN / 16;
   const size_t tile_base = ((size_t)tm * g.tiles_n + tn) * U;
+  const uint64_t t_start = (c.span_ns != nullptr && leader) ? globaltimer_ns() : 0;
+  uint64_t t0 = 0;   // start of this thread's current peer wait
   auto xoff = [&](int u, int half) {
     return (((tile_base + u) * 2 + half) * BM + row) * 8;
   };
-  auto rs_at = [&](int p, int src) { return c.rs[p] + ((size_t)par * c.world + src) * plane; };
-  auto flag_at = [&](int p, int kind, int src) {
-    return c.flags[p] + ((size_t)((kind * 2 + par) * c.world + src)) * c.max_ctas + cta;
+  auto rs_at = [&](int p, int src) { return c.rs[p] + ((size_t)c.par * W + src) * plane; };
+  auto ag_at = [&](int p) { return c.ag[p] + (size_t)c.par * plane; };
+  auto owner = [&](int u) { return (int)((tile_base + u) % (size_t)W); };
+  auto push = [&](__nv_bfloat16* base, int u, const unsigned long long* w) {
+    st_pkt(base + xoff(u, 0), w[0], w[1]);
+    st_pkt(base + xoff(u, 1), w[2], w[3]);
   };
-  auto put16 = [&](__nv_bfloat16* base, int u, const float* v) {
-    uint4 lo, hi;
-    pack_bf16x16(v, lo, hi);
-    *reinterpret_cast<uint4*>(base + xoff(u, 0)) = lo;
-    *reinterpret_cast<uint4*>(base + xoff(u, 1)) = hi;
+  // v = sum over sources s (rank order) of unit u in buffer src(s); every
+  // packet is polled until it has landed, then reset to the sentinel.  The
+  // loads of up to 4 sources are in flight at once.
+  auto recv_sum = [&](auto src, int nsrc, int u, float* v) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+#pragma unroll
+    for (int s0 = 0; s0 < TB_MAX_RANKS; s0 += 4) {
+      if (s0 < nsrc) {
+        unsigned long long d[4][4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (s0 + k < nsrc) {
+            ld_pkt(src(s0 + k) + xoff(u, 0), d[k][0], d[k][1]);
+            ld_pkt(src(s0 + k) + xoff(u, 1), d[k][2], d[k][3]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (s0 + k < nsrc) {
+            poll_pkt(src(s0 + k) + xoff(u, 0), d[k][0], d[k][1], t0);
+            poll_pkt(src(s0 + k) + xoff(u, 1), d[k][2], d[k][3], t0);
+            add_pkts(d[k], v);
+            st_pkt(src(s0 + k) + xoff(u, 0), TB_SENTINEL, TB_SENTINEL);
+            st_pkt(src(s0 + k) + xoff(u, 1), TB_SENTINEL, TB_SENTINEL);
+          }
+        }
+      }
+    }
   };
 
   // 1. push this rank's partials
@@ -441,54 +418,23 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
     const int n = tn * BN + u * 16;
     if (n >= N) break;
     float v[16];
-    acc.load16(u, u / n_own, v);
+    acc.load16(u, u / n_own, v);   // warp-collective: every lane of the warp
     if (!valid) continue;
+    unsigned long long w[4];
+    pack_pkts(v, w);
     if (c.two_shot) {
-      put16(rs_at(row_owner, c.rank), u, v);
+      push(rs_at(owner(u), c.rank), u, w);
     } else {
-      for (int p = 0; p < c.world; ++p) put16(rs_at(p, c.rank), u, v);
+      for (int p = 0; p < W; ++p) push(rs_at(p, c.rank), u, w);
     }
   }
-  // the accumulator has been read: a persistent CTA's MMA warp may reuse it
-  if (acc_free != nullptr) tc_fence_before();
-  epi_bar();
-  if (acc_free != nullptr && leader) mbar_arrive(acc_free);
-  if (flag_warp) {
-    if (leader) trace_at(g, TR_PUSHED);
-    exchange_flags(c, [&](int p) { return flag_at(p, 0, c.rank); },
-                   [&](int s) { return flag_at(c.rank, 0, s); }, epoch);
-    if (leader) trace_at(g, TR_PARTNERS);
+  if (acc_free != nullptr) {
+    // the accumulator has been read: a persistent CTA's MMA warp may reuse it
+    tc_fence_before();
+    epi_bar();
+    if (leader) mbar_arrive(acc_free);
   }
-  epi_bar();
-
-  // the world partials of unit u summed in rank order; the next rank's loads
-  // are in flight while the current rank's are added
-  auto sum_partials = [&](int u, float* v) {
-    uint4 cur0, cur1, nxt0, nxt1;
-    cur0 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, 0) + xoff(u, 0)));
-    cur1 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, 0) + xoff(u, 1)));
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = 0.f;
-    for (int s = 0; s < c.world; ++s) {
-      if (s + 1 < c.world) {
-        nxt0 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, s + 1) + xoff(u, 0)));
-        nxt1 = __ldcg(reinterpret_cast<const uint4*>(rs_at(c.rank, s + 1) + xoff(u, 1)));
-      }
-      const __nv_bfloat162* q0 = reinterpret_cast<const __nv_bfloat162*>(&cur0);
-      const __nv_bfloat162* q1 = reinterpret_cast<const __nv_bfloat162*>(&cur1);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = __bfloat1622float2(q0[i]);
-        const float2 b = __bfloat1622float2(q1[i]);
-        v[2 * i] += a.x;
-        v[2 * i + 1] += a.y;
-        v[8 + 2 * i] += b.x;
-        v[8 + 2 * i + 1] += b.y;
-      }
-      cur0 = nxt0;
-      cur1 = nxt1;
-    }
-  };
+  if (leader) trace_at(g, TR_PUSHED);
 
   const int dst = (valid && g.row_dst != nullptr) ? g.row_dst[m] : -1;
   float ss = 0.f;
@@ -498,39 +444,36 @@ __device__ __forceinline__ float run_resid_tp(const GemmArgs& g, const AccReader
                         [&](int u, int n, const float* h_old, const uint32_t* g8) {
                           if (!valid) return;
                           float v[16];
-                          sum_partials(u, v);
+                          recv_sum([&](int s) { return rs_at(c.rank, s); }, W, u, v);
                           ss += resid_update(g, m, n, dst, v, h_old, g8);
                         });
-    return ss;
+  } else {
+    // 2'. owners reduce their units and send the bf16 sums to every rank
+    for (int u = own; u < U; u += n_own) {
+      const int n = tn * BN + u * 16;
+      if (n >= N) break;
+      if (!valid || owner(u) != c.rank) continue;
+      float v[16];
+      recv_sum([&](int s) { return rs_at(c.rank, s); }, W, u, v);
+      unsigned long long w[4];
+      pack_pkts(v, w);
+      for (int p = 0; p < W; ++p) push(ag_at(p), u, w);
+    }
+    if (leader) trace_at(g, TR_PARTNERS);
+    // 3. every rank applies the same reduced sums
+    for_resid_units<BN>(g, m, tn, own, n_own, pre,
+                        [&](int u, int n, const float* h_old, const uint32_t* g8) {
+                          if (!valid) return;
+                          float v[16];
+                          recv_sum([&](int) { return ag_at(c.rank); }, 1, u, v);
+                          ss += resid_update(g, m, n, dst, v, h_old, g8);
+                        });
   }
-
-  // 2'. owners reduce their rows and broadcast the bf16 sums
-  const size_t ag_off = (size_t)par * plane;
-  for (int u = own; u < U; u += n_own) {
-    const int n = tn * BN + u * 16;
-    if (n >= N) break;
-    if (!valid || row_owner != c.rank) continue;
-    float v[16];
-    sum_partials(u, v);
-    for (int p = 0; p < c.world; ++p) put16(c.ag[p] + ag_off, u, v);
+  if (c.span_ns != nullptr) {
+    epi_bar();   // every row of the tile has its values
+    if (leader) atomicMax(c.span_ns, (unsigned long long)(globaltimer_ns() - t_start));
   }
-  epi_bar();
-  if (flag_warp) {
-    exchange_flags(c, [&](int p) { return flag_at(p, 1, c.rank); },
-                   [&](int s) { return flag_at(c.rank, 1, s); }, epoch);
-    if (leader) trace_at(g, TR_SUMS);
-  }
-  epi_bar();
-  // 3. every rank applies the same reduced sums
-  for_resid_units<BN>(g, m, tn, own, n_own, pre,
-                      [&](int u, int n, const float* h_old, const uint32_t* g8) {
-                        if (!valid) return;
-                        float v[16];
-                        const __nv_bfloat16* src = c.ag[c.rank] + ag_off;
-                        ld_bf16x8_cg(src + xoff(u, 0), v);
-                        ld_bf16x8_cg(src + xoff(u, 1), v + 8);
-                        ss += resid_update(g, m, n, dst, v, h_old, g8);
-                      });
+  if (leader) trace_at(g, TR_SUMS);
   return ss;
 }
 
@@ -969,8 +912,7 @@ __device__ __forceinline__ void finish(const GemmArgs& g, const RowStage& rw, co
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
-                   const __grid_constant__ CUtensorMap tma_b,
-                   const __grid_constant__ CUtensorMap tma_pf, const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tma_b, const GemmArgs g) {
   using L = GemmLayout<BN, STAGES>;
   constexpr uint32_t TCOLS = tmem_cols(BN);
   extern __shared__ uint8_t smem_raw[];
@@ -1119,7 +1061,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (threadIdx.x == 64) trace_at(g, TR_CLUSTER_SYNC);
     if (warp >= 2) {
       if (tp) {
-        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, z, S, pre, blockIdx.x, nullptr);
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, z, S, pre, nullptr);
         store_row_sumsq(g, tm, tn * S + z, row, ss);
       } else {
         float ss[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1158,7 +1100,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     if (run) {
       if (tp) {
-        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre, blockIdx.x, nullptr);
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre, nullptr);
         store_row_sumsq(g, tm, tn, row, ss);
       } else {
         stage_global<BN>(acc, tu, smem, nslot, row);
@@ -1170,11 +1112,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     if (threadIdx.x == 64) trace_at(g, TR_END);
   }
-  // warp 0: warm L2 with the next kernel's weights while this CTA finishes
-  if (warp == 0 && g.pf.base != nullptr) {
-    if (mode == SPLIT_CLUSTER || mbar_wait(done, 0)) l2_prefetch_share(g.pf, &tma_pf, lane);
-  }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1346,7 +1283,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       acc.taddr = tmem_base + (uint32_t)(b * TC) + ((uint32_t)(q * 32) << 16);
       if (tp) {
-        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre, tile, &acc_empty[b]);
+        const float ss = run_resid_tp<BN>(g, acc, tm, tn, row, 0, 1, pre, &acc_empty[b]);
         store_row_sumsq(g, tm, tn, row, ss);
         continue;
       }
@@ -1388,16 +1325,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // ------------------------------------------------------------------ host side
 
 template <int BN, int STAGES, int EPI>
-static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const CUtensorMap& tpf,
-                     const GemmArgs& g, cudaStream_t stream) {
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const GemmArgs& g,
+                     cudaStream_t stream) {
   using L = GemmLayout<BN, STAGES>;
   auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-    if (e != cudaSuccess) return host_err(e, "gemm smem attribute");
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> attr_devs{0};
+  if (int rc = smem_attr_once(kern, L::SMEM, attr_devs, "gemm smem attribute")) return rc;
   const int tiles = g.tiles_m * g.tiles_n;
   if (g.splits > 1 && g.ws == nullptr) {  // cluster split-K: a tile's splits are one cluster along x
     const bool paired = EPI == EPI_SWIGLU || (EPI == EPI_QKV && g.head_dim >= 32);
@@ -1405,10 +1338,10 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb_, const CUtens
     if (cluster_region_bytes(np, cp, g.splits) > L::RING)
       return arg_err("cluster split-K: the partial chunks of this (bn, splits) do not fit shared memory");
     return launch_pdl(kern, dim3(tiles * g.splits), dim3(GEMM_THREADS), L::SMEM, stream,
-                      g.splits, "gemm cluster launch", ta, tb_, tpf, g);
+                      g.splits, "gemm cluster launch", ta, tb_, g);
   }
   return launch_pdl(kern, dim3(tiles, g.splits), dim3(GEMM_THREADS), L::SMEM, stream, 1,
-                    "gemm launch", ta, tb_, tpf, g);
+                    "gemm launch", ta, tb_, g);
 }
 
 static int num_sms() {
@@ -1429,12 +1362,9 @@ static int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb_, cons
                              cudaStream_t stream) {
   using L = PersistLayout<BN, STAGES>;
   auto kern = gemm_persistent_kernel<BN, STAGES, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-    if (e != cudaSuccess) return host_err(e, "persistent gemm smem attribute");
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> attr_devs{0};
+  if (int rc = smem_attr_once(kern, L::SMEM, attr_devs, "persistent gemm smem attribute"))
+    return rc;
   const int tiles = g.tiles_m * g.tiles_n;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   return launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), L::SMEM, stream, 1,
@@ -1442,8 +1372,8 @@ static int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb_, cons
 }
 
 template <int EPI>
-static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_,
-                      const CUtensorMap& tpf, const GemmArgs& g, cudaStream_t stream) {
+static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_, const GemmArgs& g,
+                      cudaStream_t stream) {
   if (g.splits == 1 && g.ws == nullptr) {   // no split-K: persistent tiles
     switch (bn) {
       case 64: return launch_persistent<64, 7, EPI>(ta, tb_, g, stream);
@@ -1454,10 +1384,10 @@ static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb_,
     }
   }
   switch (bn) {
-    case 64: return launch_bn<64, 8, EPI>(ta, tb_, tpf, g, stream);
-    case 128: return launch_bn<128, 6, EPI>(ta, tb_, tpf, g, stream);
-    case 192: return launch_bn<192, 5, EPI>(ta, tb_, tpf, g, stream);
-    case 256: return launch_bn<256, 4, EPI>(ta, tb_, tpf, g, stream);
+    case 64: return launch_bn<64, 8, EPI>(ta, tb_, g, stream);
+    case 128: return launch_bn<128, 6, EPI>(ta, tb_, g, stream);
+    case 192: return launch_bn<192, 5, EPI>(ta, tb_, g, stream);
+    case 256: return launch_bn<256, 4, EPI>(ta, tb_, g, stream);
     default: return arg_err("bn must be 64, 128, 192 or 256");
   }
 }
@@ -1494,22 +1424,6 @@ int gemm_max_active_clusters(int bn, int cluster, int* out) {
 
 unsigned long long* g_debug_trace = nullptr;
 
-int gemm_set_prefetch(GemmArgs& g, const tb_l2_prefetch* p) {
-  g.pf = L2Prefetch{};
-  if (p == nullptr || p->base == nullptr) return TB_OK;
-  if (reinterpret_cast<uintptr_t>(p->base) % 16 || p->ld % 8 || p->bytes % 16 || p->rows <= 0 ||
-      p->k <= 0 || p->ld < p->k || p->splits < 1 || p->bytes < 0)
-    return arg_err("l2 prefetch: base 16-byte aligned, ld >= k and a multiple of 8, "
-                   "bytes a multiple of 16, rows/k/splits positive");
-  g.pf.base = static_cast<const char*>(p->base);
-  g.pf.ld = p->ld;
-  g.pf.rows = p->rows;
-  g.pf.k = p->k;
-  g.pf.splits = p->splits;
-  g.pf.bytes = p->bytes;
-  return TB_OK;
-}
-
 int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb, GemmArgs g,
                 cudaStream_t stream) {
   g.trace = g_debug_trace;
@@ -1536,24 +1450,12 @@ int gemm_launch(int epi, int bn, const void* A, int lda, const void* B, int ldb,
   if (rc) return rc;
   rc = make_tmap_2d(&tbm, B, g.K, g.N, (uint64_t)ldb * 2, BK, bn);
   if (rc) return rc;
-  // L2 warm-up map of the next weight: unswizzled 256 x 256 boxes
-  CUtensorMap tpf;
-  memset(&tpf, 0, sizeof(tpf));
-  if (g.pf.base != nullptr) {
-    const uint32_t bc = (uint32_t)min(PF_BOX, g.pf.k / 8 * 8), br = (uint32_t)min(PF_BOX, g.pf.rows);
-    if (bc < 8 || g.pf.bytes < 16) {
-      g.pf = L2Prefetch{};
-    } else {
-      rc = make_tmap_2d(&tpf, g.pf.base, g.pf.k, g.pf.rows, (uint64_t)g.pf.ld * 2, bc, br, false);
-      if (rc) return rc;
-    }
-  }
   switch (epi) {
-    case EPI_F32: return launch_epi<EPI_F32>(bn, ta, tbm, tpf, g, stream);
-    case EPI_BF16: return launch_epi<EPI_BF16>(bn, ta, tbm, tpf, g, stream);
-    case EPI_QKV: return launch_epi<EPI_QKV>(bn, ta, tbm, tpf, g, stream);
-    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(bn, ta, tbm, tpf, g, stream);
-    case EPI_RESID: return launch_epi<EPI_RESID>(bn, ta, tbm, tpf, g, stream);
+    case EPI_F32: return launch_epi<EPI_F32>(bn, ta, tbm, g, stream);
+    case EPI_BF16: return launch_epi<EPI_BF16>(bn, ta, tbm, g, stream);
+    case EPI_QKV: return launch_epi<EPI_QKV>(bn, ta, tbm, g, stream);
+    case EPI_SWIGLU: return launch_epi<EPI_SWIGLU>(bn, ta, tbm, g, stream);
+    case EPI_RESID: return launch_epi<EPI_RESID>(bn, ta, tbm, g, stream);
     default: return arg_err("unknown epilogue");
   }
 }

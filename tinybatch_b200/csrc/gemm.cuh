@@ -38,37 +38,30 @@ enum EpiKind : int {
 constexpr int TB_MAX_RANKS = 8;
 
 // Device view of a tensor-parallel communicator (comm.cu).  Every rank owns
-// one allocation with the same layout; rs/ag/flags[p] point into rank p's
+// one allocation with the same layout; rs/ag/am[p] point into rank p's
 // allocation (peer-mapped for p != rank).
-//   rs[p]    [2 parity][world src][plane] bf16: partial sums pushed by each
-//            source rank (one-shot: every column; two-shot: the columns rank
-//            p owns); a plane holds a whole output tile by tile, each tile as
-//            [16-column unit][half][128 rows][8 columns]
-//   ag[p]    [2 parity][plane] bf16: reduced sums (two-shot)
-//   flags[p] [2 kind][2 parity][world src][max_ctas] u32: "source src's CTA
-//            c has delivered call `epoch`" (kind 0: partials, 1: sums)
-//   state    this rank's step counter; a call's epoch is
-//            state[0] * n_sites + site + 1, its parity epoch & 1
+//   rs[p]  [2 parity][world src][plane] bf16: partials pushed by each source
+//          rank (one-shot: every column of every row; two-shot: the rows
+//          rank p owns); a plane holds a whole output tile by tile, each tile
+//          as [16-column unit][half][128 rows][8 columns]
+//   ag[p]  [2 parity][plane] bf16: reduced sums (two-shot)
+//   am[p]  [2 parity][world src][max_rows] u64: argmax candidates
+// No flags: every buffer holds the all-ones sentinel word (TB_SENTINEL) until
+// a peer stores data into it with 8-byte-atomic stores, the receiver polls
+// the data words themselves and puts the sentinel back once it has read
+// them.  A call's parity (seq & 1) picks the buffer half; consecutive calls
+// of one kind alternate parity, so a rank can only write a half again after
+// every rank has finished reading it (each call needs every rank's data,
+// and a rank pushes call seq+1's data only after its call seq completed).
 struct CommDev {
   int rank, world;  // world <= 1: no all-reduce
   int two_shot;
-  int site, n_sites;
-  int max_rows, n_cols, max_ctas;
-  uint32_t* state;
+  int par;          // parity of this call (seq & 1)
+  int max_rows, n_cols;
+  unsigned long long* span_ns;  // optional: max over CTAs of the exchange span
   __nv_bfloat16* rs[TB_MAX_RANKS];
   __nv_bfloat16* ag[TB_MAX_RANKS];
-  uint32_t* flags[TB_MAX_RANKS];
-};
-
-// An L2 warm-up request for the weight the next kernel streams: a bf16
-// matrix [rows, k] with row pitch ld elements, read by `splits` K segments
-// (split-K boundaries of 64-column blocks); the first `bytes` of every
-// (row, segment) are prefetched, in 256 x 256 tensor boxes (the kernel's
-// third tensor map).  base == nullptr: none.
-struct L2Prefetch {
-  const char* base;
-  long long ld;
-  int rows, k, splits, bytes;
+  unsigned long long* am[TB_MAX_RANKS];
 };
 
 struct GemmArgs {
@@ -111,8 +104,6 @@ struct GemmArgs {
   CommDev comm;
   // debug timeline (tb_debug_trace): per CTA 16 globaltimer stamps, or null
   unsigned long long* trace;
-  // issued by warp 0 once this CTA's main loop is done
-  L2Prefetch pf;
 };
 
 // Timeline points recorded when GemmArgs::trace is set.
@@ -120,9 +111,9 @@ enum TracePoint : int {
   TR_START = 0,       // CTA set up (barriers, TMEM)
   TR_LOADS_ISSUED,    // producer issued its last TMA load
   TR_ACC_READY,       // epilogue saw the accumulator complete
-  TR_PUSHED,          // partials pushed and fenced (all-reduce)
-  TR_PARTNERS,        // partner flags observed (all-reduce)
-  TR_SUMS,            // reduced sums delivered (two-shot)
+  TR_PUSHED,          // partials pushed (all-reduce)
+  TR_PARTNERS,        // every source's partials received (all-reduce)
+  TR_SUMS,            // reduced sums received (two-shot)
   TR_END,             // epilogue done
   TR_PARKED,          // cluster split: partial chunks stored to their owners
   TR_CLUSTER_SYNC,    // cluster split: every member's chunks arrived
@@ -130,8 +121,5 @@ enum TracePoint : int {
   TR_COMBINED,        // residual finisher: first chunk updated (warp 2)
   TR_POINTS = 16,
 };
-
-// Host side (gemm.cu): validate and copy an L2 warm-up request into g.
-int gemm_set_prefetch(GemmArgs& g, const tb_l2_prefetch* p);
 
 }  // namespace tb

@@ -47,6 +47,34 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+int current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  if (get_cur == nullptr || get_id == nullptr) {
+    void* p = nullptr;
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r1, r2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r1) != cudaSuccess ||
+        r1 != cudaDriverEntryPointSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &q, cudaEnableDefault, &r2) != cudaSuccess ||
+        r2 != cudaDriverEntryPointSuccess) {
+      set_last_error("cuCtxGetCurrent / cuCtxGetId entry points unavailable");
+      return TB_ERR_CUDA;
+    }
+    get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    get_id = reinterpret_cast<CtxGetIdFn>(q);
+  }
+  CUcontext ctx = nullptr;
+  if (get_cur(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, id) != CUDA_SUCCESS) {
+    set_last_error("no current CUDA context");
+    return TB_ERR_CUDA;
+  }
+  return TB_OK;
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                  uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_rows,
                  bool swizzle) {

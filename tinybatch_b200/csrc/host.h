@@ -8,6 +8,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #include "../../include/tinybatch_b200.h"
@@ -19,6 +20,10 @@ namespace tb {
 int host_err(cudaError_t e, const char* what);
 int arg_err(const char* what);
 void set_last_error(const char* fmt, ...);
+
+// Unique id of the calling thread's current CUDA context (changes when a
+// device's primary context is reset and created again).
+int current_context_id(unsigned long long* id);
 
 // 2-D bf16 tensor map over a row-major [rows, inner] matrix with the given
 // row pitch, box {box_inner, box_rows}, 128-byte swizzle (or none, for maps
@@ -52,6 +57,27 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
   cfg.attrs = attr;
   cfg.numAttrs = n;
   return host_err(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
+}
+
+// Kernel attributes are per device: `devs` (one static per kernel at the
+// call site) records, one bit per device index, where `kern`'s dynamic
+// shared-memory limit (and, with max_carveout, its shared-memory carveout)
+// has been set.  Concurrent first calls may both set it, which is harmless.
+template <typename... KArgs>
+int smem_attr_once(void (*kern)(KArgs...), int bytes, std::atomic<unsigned long long>& devs,
+                   const char* what, bool max_carveout = false) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return host_err(e, what);
+  const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+  if (bit && (devs.load(std::memory_order_acquire) & bit)) return 0;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && max_carveout)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return host_err(e, what);
+  devs.fetch_or(bit, std::memory_order_release);
+  return 0;
 }
 
 struct GemmArgs;

@@ -14,7 +14,8 @@
 // names a shadow object), so the first call on each device, with that
 // device current, asks the runtime for the real address with
 // cudaGetSymbolAddress and caches it.  Make that first call before any
-// stream capture.
+// stream capture.  The cache remembers the context it was resolved in: after
+// a device reset (a new primary context) the next call resolves it again.
 //
 // All calls on a device share the array and it keeps whatever the last call
 // left there.  The arrival counters at its head must start at zero, so each
@@ -39,20 +40,30 @@ static __device__ __align__(256) unsigned char g_static_scratch[TB_STATIC_SCRATC
 
 constexpr int MAX_DEVICES = 64;
 static void* g_static_ptr[MAX_DEVICES] = {};
+static unsigned long long g_static_ctx[MAX_DEVICES] = {};
 static std::mutex g_static_mu;
 
-// Device address of g_static_scratch on the current device (resolved once).
+// Device address of g_static_scratch on the current device (resolved once
+// per device and context).
 static int static_scratch_ptr(void** out) {
   int dev = -1;
   int rc = host_err(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc) return rc;
   if (dev < 0 || dev >= MAX_DEVICES) return arg_err("device index beyond 64");
+  unsigned long long ctx = 0;
+  if (current_context_id(&ctx) != TB_OK) {
+    // no context current on this thread yet: make the device's primary one current
+    rc = host_err(cudaSetDevice(dev), "cudaSetDevice");
+    if (!rc) rc = current_context_id(&ctx);
+    if (rc) return rc;
+  }
   std::lock_guard<std::mutex> lock(g_static_mu);
-  if (g_static_ptr[dev] == nullptr) {
+  if (g_static_ptr[dev] == nullptr || g_static_ctx[dev] != ctx) {
     void* p = nullptr;
     rc = host_err(cudaGetSymbolAddress(&p, g_static_scratch), "cudaGetSymbolAddress(scratch)");
     if (rc) return rc;
     g_static_ptr[dev] = p;
+    g_static_ctx[dev] = ctx;
   }
   *out = g_static_ptr[dev];
   return TB_OK;
@@ -65,7 +76,8 @@ extern "C" int tb_linear_static_scratch(const void* x, int ldx, const void* w, i
                                         float inv_d, float eps, void* out, int ld_out,
                                         int out_f32, int bn, int splits, void* stream) {
   using namespace tb;
-  if (bn != 64 && bn != 128 && bn != 256) return arg_err("bn must be 64, 128 or 256");
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256)
+    return arg_err("bn must be 64, 128, 192 or 256");
   if (out == nullptr || ld_out < N || (out_f32 ? ld_out % 4 : ld_out % 8))
     return arg_err("out / ld_out");
   if (M <= 0 || N <= 0 || splits < 1) return arg_err("M, N > 0 and splits >= 1 required");

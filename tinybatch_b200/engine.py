@@ -15,9 +15,14 @@ decoding sequence) -> forward -> sample -> append / finish.  Differences:
   batch, ``step`` queues the next decode step on the device (its token ids
   copied there from this step's argmax) before reading this step's tokens
   back, so the host's scheduling and output handling run while the GPU
-  computes.  Every request produces the same tokens as without it; a
-  sequence that stops at step k had step k+1 computed for nothing (its
-  output is dropped, its blocks freed);
+  computes.  Every request produces the same tokens and the same block
+  tables as without it: a sequence that stops on a stop token at step k had
+  step k+1 computed for nothing (its output is dropped), and the blocks step
+  k+1 reserved are taken back and reserved again in the reference's order
+  (the stopped sequence's blocks freed first).  A step reserves the slot of
+  the position after the one it writes (``append_slot`` sees the token list
+  that already holds the token being processed), so step k+1 wrote no KV
+  into the blocks it reserved and nothing on the device moves;
 * a prompt whose length is a multiple of the block size gets the block for
   its first decode token here.  The reference scheduler reserves the slot
   *after* the token being written (``append_slot`` sees the token list that
@@ -63,6 +68,10 @@ class _InFlight:
     host_ids: torch.Tensor    # pinned int32, filled by an asynchronous copy
     done: torch.cuda.Event    # recorded after that copy
     h2d_bytes: int
+    # every running sequence's block-table length before this step was
+    # scheduled, in scheduling order (to redo the step's block reservations
+    # in the reference's order when an earlier step's sequence stops)
+    tables_before: list = field(default_factory=list)
 
 
 class LLMEngine:
@@ -244,7 +253,7 @@ class LLMEngine:
                 return self._step_plain(None)
             self._inflight = self._launch(None)
         nxt = self._launch(self._inflight) if self._overlap_ready(self._inflight) else None
-        out = self._collect(self._inflight)
+        out = self._collect(self._inflight, nxt)
         if nxt is not None and all(r.status is Status.FINISHED for r in nxt.reqs):
             self._collect(nxt)          # every sequence of it has stopped
             nxt = None
@@ -287,6 +296,7 @@ class LLMEngine:
         for it.  With ``prev`` (the step queued before it, same sequences in
         the same order) the token ids are ``prev``'s samples, copied on the
         device; the host holds PENDING for them."""
+        before = [(r, len(r.block_table)) for r in self.scheduler.running]
         batch = self.scheduler.schedule()
         reqs = batch.decode
         if batch.prefill or not reqs:
@@ -318,32 +328,72 @@ class LLMEngine:
             r.output_token_ids.append(PENDING)
         self.last_batch = None
         self.last_logits = None
-        return _InFlight(reqs, slots, host, done, md.h2d_bytes)
+        return _InFlight(reqs, slots, host, done, md.h2d_bytes, before)
 
-    def _collect(self, f: _InFlight) -> list[StepOutput]:
+    def _collect(self, f: _InFlight, queued: _InFlight | None = None) -> list[StepOutput]:
         """Wait for a queued step's tokens and apply them (append / finish) as
-        ``step`` does; sequences that stopped at an earlier step are skipped."""
+        ``step`` does; sequences that stopped at an earlier step are skipped.
+        ``queued``: the step already queued after ``f``; when a sequence
+        stops here, its block reservations are redone in the reference's
+        order (``_rereserve``)."""
         f.done.synchronize()
         toks = f.host_ids[: len(f.reqs)].tolist()
         self.last_h2d_bytes = f.h2d_bytes
         self.last_d2h_bytes = 4 * len(f.reqs)
         now = time.perf_counter()
         lim = self.cfg.max_model_len
-        outputs: list[StepOutput] = []
+        rows = []
         for req, idx, tok in zip(f.reqs, f.slots, toks):
             if req.status is Status.FINISHED:
                 continue
+            finished = (tok in self.eos_ids or idx + 1 >= req.max_new_tokens
+                        or len(req.prompt_token_ids) + idx + 1 >= lim)
+            rows.append((req, idx, tok, finished))
+        redo = queued is not None and any(fin for *_, fin in rows)
+        if redo:
+            self._take_back(queued)
+        outputs: list[StepOutput] = []
+        for req, idx, tok, finished in rows:
             req.output_token_ids[idx] = tok
             if req.first_token_time is None:
                 req.first_token_time = now
-            finished = (tok in self.eos_ids or idx + 1 >= req.max_new_tokens
-                        or len(req.prompt_token_ids) + idx + 1 >= lim)
             delta = self.tokenizer.decode([tok], skip_special_tokens=True) if self.tokenizer else ""
             if finished:
                 del req.output_token_ids[idx + 1:]     # a later queued step's token
                 self.scheduler.finish(req)
             outputs.append(StepOutput(req.req_id, tok, delta, finished, req))
+        if redo:
+            self._rereserve(queued)
         return outputs
+
+    def _take_back(self, q: _InFlight) -> None:
+        """Undo the block reservations of queued step ``q``: its scheduling
+        only popped fresh blocks from the top of the free stack (a decode
+        step with prefix caching off and no preemption), so pushing each
+        table's new tail back, last first, restores the stack exactly."""
+        bm = self.block_manager
+        for req, n in reversed(q.tables_before):
+            while len(req.block_table) > n:
+                bid = req.block_table.pop()
+                blk = bm.blocks[bid]
+                blk.ref_count = 0
+                blk.token_ids = []
+                bm.free_ids.append(bid)
+
+    def _rereserve(self, q: _InFlight) -> None:
+        """Reserve queued step ``q``'s blocks again, as the reference's next
+        schedule does after the stopped sequences were freed: ``append_slot``
+        per running sequence in order, plus ``build_batch``'s extension.
+        ``q`` wrote its KV at the position before the reserved one, inside
+        blocks the tables already held, so its device work stays valid."""
+        bm, bs = self.block_manager, self.cfg.block_size
+        for req, _ in q.tables_before:
+            if req.status is not Status.RUNNING:
+                continue
+            L = req.context_len() - 1          # q's own token is still pending
+            bm.append_slot(req.block_table, req.token_view(L))
+            if len(req.block_table) * bs < L:
+                bm.append_slot(req.block_table, req.token_view(L - 1))
 
     def decode_graph(self, n: int, ctx_total: int | None = None) -> DecodeGraph:
         """The captured decode step for ``n`` sequences (captured on first

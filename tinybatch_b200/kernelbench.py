@@ -83,12 +83,10 @@ def build(tp: int, layers: int, device: torch.device):
     return cfg, model, cache, md
 
 
-def run(tp: int = 1, layers: int = 1, reps: int = 5, l2_mb: float | None = None,
+def run(tp: int = 1, layers: int = 1, reps: int = 5,
         split_tokens: int | None = None) -> list[dict]:
     dev = torch.device("cuda", torch.cuda.current_device())
     cfg, model, cache, md = build(tp, layers, dev)
-    if l2_mb is not None:
-        model.dm.l2_prefetch_bytes = int(l2_mb * (1 << 20))
     model.dm.split_tokens = split_tokens
     for _ in range(2):
         model.forward_meta(md, cache, sample=True)
@@ -122,7 +120,6 @@ def run(tp: int = 1, layers: int = 1, reps: int = 5, l2_mb: float | None = None,
     _native.raise_on_status("kernelbench")
     pk, src = peaks()
     rows = [{"kernel": "forward", "tp": tp, "layers": layers,
-             "l2_prefetch_mb": model.dm.l2_prefetch_bytes >> 20,
              "split_tokens": split_tokens or "auto", "launches_per_step": 1,
              "us_per_launch": round(statistics.median(fwd), 2)}]
     for kind, ts in times.items():
@@ -131,8 +128,7 @@ def run(tp: int = 1, layers: int = 1, reps: int = 5, l2_mb: float | None = None,
         t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
         t_tc = flops / (pk["bf16_tflops"] * 1e12)
         bound = "hbm" if t_hbm >= t_tc else "tensor"
-        rows.append({"kernel": kind, "tp": tp, "l2_prefetch_mb": model.dm.l2_prefetch_bytes >> 20,
-                     "launches_per_step": n, "us_per_launch": round(us, 2),
+        rows.append({"kernel": kind, "tp": tp, "launches_per_step": n, "us_per_launch": round(us, 2),
                      "bytes_per_launch": int(nbytes), "GBps": round(nbytes / us / 1e3, 1),
                      "TFLOPs": round(flops / us / 1e6, 1), "bound": bound,
                      "us_roofline": round(max(t_hbm, t_tc) * 1e6, 2),
@@ -146,18 +142,14 @@ def main() -> None:
     ap.add_argument("--tp", type=int, default=1, help="shard as rank 0 of this many ranks")
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--reps", type=int, default=5)
-    ap.add_argument("--l2-mb", default=None,
-                    help="MiB of the next weight warmed into L2 per GEMM; comma list to sweep")
     ap.add_argument("--split-tokens", default=None,
                     help="decode split-KV size (default: the runtime's policy); comma list")
     args = ap.parse_args()
-    sweep = [None] if args.l2_mb is None else [float(v) for v in args.l2_mb.split(",")]
     splits = [None] if args.split_tokens is None else [int(v) or None for v in
                                                        args.split_tokens.split(",")]
-    for mb in sweep:
-        for st in splits:
-            for r in run(args.tp, args.layers, args.reps, mb, st):
-                print(json.dumps(r), flush=True)
+    for st in splits:
+        for r in run(args.tp, args.layers, args.reps, st):
+            print(json.dumps(r), flush=True)
 
 
 if __name__ == "__main__":

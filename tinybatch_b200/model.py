@@ -11,8 +11,6 @@ There is no CPU path: the model lives on a CUDA device and every op runs in
 """
 from __future__ import annotations
 
-import json
-
 import torch
 
 from . import _native
@@ -31,23 +29,18 @@ class Qwen2Paged:
     """Weights + forward.  Inference only."""
 
     def __init__(self, model_id: str, device: torch.device | str = "cuda",
-                 dtype: torch.dtype = torch.bfloat16):
+                 dtype: torch.dtype = torch.bfloat16, rank: int = 0, world: int = 1,
+                 comm=None, **kw):
         """Load a HF Qwen2 checkpoint (config.json + *.safetensors) from a
-        local directory or the hub cache, as the reference does."""
-        import glob
-        import os
-
-        from safetensors.torch import load_file
-        path = model_id
-        if not os.path.isdir(path):
-            from huggingface_hub import snapshot_download
-            path = snapshot_download(model_id, allow_patterns=["*.json", "*.safetensors"])
-        with open(os.path.join(path, "config.json")) as f:
-            cfg = ModelConfig.from_hf(json.load(f))
-        raw: dict[str, torch.Tensor] = {}
-        for shard in sorted(glob.glob(os.path.join(path, "*.safetensors"))):
-            raw.update(load_file(shard))
-        self._setup(cfg, raw, device, dtype, rank=0, world=1, comm=None)
+        local directory or the hub cache, as the reference does
+        (``src/tinybatch/model.py:86-98``).  With ``world`` > 1 this process
+        is tensor-parallel rank ``rank``: it reads only its own slices of the
+        checkpoint (``checkpoint.load_rank_weights``)."""
+        from .checkpoint import load_config, load_rank_weights, resolve
+        path = resolve(model_id)
+        cfg = load_config(path)
+        w = load_rank_weights(path, cfg, rank, world, device, dtype)
+        self._setup(cfg, w, device, dtype, rank=rank, world=world, comm=comm, sharded=True, **kw)
 
     @classmethod
     def from_weights(cls, cfg: ModelConfig, w: dict, device: torch.device | str = "cuda",

@@ -1,5 +1,6 @@
 """Op-level sweep of the fused row-parallel GEMM + all-reduce + residual +
-RMSNorm prologue.
+RMSNorm prologue: M in {1, 8, 64, 512, 4096} rows, (K, N) in the Qwen2.5-14B
+and -72B row-parallel shapes, over t tensor-parallel ranks.
 
     torchrun --nproc-per-node T -m tinybatch_b200.opbench [--rows 1,8,64,512,4096]
 
@@ -84,6 +85,7 @@ def _time_graph(fn, reps: int, world: int) -> float:
 
 
 def run(ms: list[int], shapes=SHAPES, reps: int = 20, two_shot: bool | None = None) -> list[dict]:
+    assert reps % 2 == 0, "an even number of calls per graph keeps the parities alternating"
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -109,15 +111,17 @@ def run(ms: list[int], shapes=SHAPES, reps: int = 20, two_shot: bool | None = No
             t_fused = None
             if comm is not None:
                 def fused(i):
-                    if i == 0:
-                        comm.begin_step()
-                    comm.row_linear_residual(x, w, h, gn, hg, sq, site=i, n_sites=reps, bn=bn,
-                                             splits=splits, two_shot=two_shot)
+                    # seq left to the communicator: consecutive calls alternate parity
+                    # (graphs of an even number of calls keep that across replays)
+                    comm.row_linear_residual(x, w, h, gn, hg, sq, bn=bn, splits=splits,
+                                             two_shot=two_shot)
                 t_fused = _time_graph(fused, reps, world)
             t = t_fused if t_fused is not None else t_plain
             t_roof, bound = roofline_s(M, K, N, world, pk)
             b_nvl = 2.0 * (world - 1) / world * 2 * M * N
+            ts = (comm.use_two_shot(M, N) if two_shot is None else two_shot) if comm else None
             out.append({"M": M, "K": K, "N": N, "tp": world, "bn": bn, "splits": splits,
+                        "two_shot": ts,
                         "us_fused": None if t_fused is None else round(t_fused * 1e6, 2),
                         "us_gemm_only": round(t_plain * 1e6, 2),
                         "us_roofline": round(t_roof * 1e6, 2), "bound": bound,

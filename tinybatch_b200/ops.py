@@ -61,7 +61,7 @@ def _sq(sq):
 
 
 def linear(x, w, out, *, sq=None, inv_d=0.0, eps=0.0, bn=128, splits=1, scratch=None,
-           split_mode="cluster", next_weight=None):
+           split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w.shape[0]
@@ -69,13 +69,13 @@ def linear(x, w, out, *, sq=None, inv_d=0.0, eps=0.0, bn=128, splits=1, scratch=
     sp, parts, sld = _sq(sq)
     N.check(lib.tb_linear(ptr(x), x.stride(0), ptr(w), w.stride(0), M, Nn, K, sp, parts, sld,
                           inv_d, eps, ptr(out), out.stride(0), int(out.dtype == torch.float32),
-                          bn, splits, ws, wsn, N.pf_arg(next_weight), N.stream_ptr()), "tb_linear")
+                          bn, splits, ws, wsn, N.stream_ptr()), "tb_linear")
     return out
 
 
 def qkv_rope_kv(x, w_qkv, bias, *, n_q_heads, n_kv_heads, head_dim, sq, inv_d, eps,
                 rope_cos, rope_sin, positions, slots, q_out, kv_pool, block_size,
-                bn=128, splits=1, scratch=None, split_mode="cluster", next_weight=None):
+                bn=128, splits=1, scratch=None, split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w_qkv.shape[0]
@@ -85,13 +85,12 @@ def qkv_rope_kv(x, w_qkv, bias, *, n_q_heads, n_kv_heads, head_dim, sq, inv_d, e
                                K, n_q_heads, n_kv_heads, head_dim, sp, parts, sld, inv_d, eps,
                                ptr(rope_cos), ptr(rope_sin), rope_cos.shape[0], ptr(positions),
                                ptr(slots), ptr(q_out), q_out.stride(0), ptr(kv_pool),
-                               block_size, bn, splits, ws, wsn, N.pf_arg(next_weight),
-                               N.stream_ptr()),
+                               block_size, bn, splits, ws, wsn, N.stream_ptr()),
             "tb_qkv_rope_kv")
 
 
 def gate_up_swiglu(x, w_gu, act, *, n_feat, sq, inv_d, eps, bn=128, splits=1, scratch=None,
-                   split_mode="cluster", next_weight=None):
+                   split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w_gu.shape[0]
@@ -99,7 +98,7 @@ def gate_up_swiglu(x, w_gu, act, *, n_feat, sq, inv_d, eps, bn=128, splits=1, sc
     sp, parts, sld = _sq(sq)
     N.check(lib.tb_gate_up_swiglu(ptr(x), x.stride(0), ptr(w_gu), w_gu.stride(0), M, K, n_feat,
                                   sp, parts, sld, inv_d, eps, ptr(act), act.stride(0), bn,
-                                  splits, ws, wsn, N.pf_arg(next_weight), N.stream_ptr()),
+                                  splits, ws, wsn, N.stream_ptr()),
             "tb_gate_up_swiglu")
     return act
 
@@ -112,7 +111,7 @@ def row_parts(n_cols: int, bn: int, splits: int, split_mode: str = "cluster") ->
 
 
 def row_linear_residual(x, w, h, g_next, hg, sq_out, *, row_dst=None, hg2=None, sq2=None,
-                        bn=128, splits=1, scratch=None, split_mode="cluster", next_weight=None):
+                        bn=128, splits=1, scratch=None, split_mode="cluster"):
     lib = N.load()
     M, K = x.shape
     Nn = w.shape[0]
@@ -121,7 +120,7 @@ def row_linear_residual(x, w, h, g_next, hg, sq_out, *, row_dst=None, hg2=None, 
         ptr(x), x.stride(0), ptr(w), w.stride(0), M, Nn, K, ptr(h), h.stride(0), ptr(g_next),
         ptr(hg), hg.stride(0), ptr(sq_out), sq_out.stride(0), ptr(row_dst), ptr(hg2),
         ptr(sq2), sq2.stride(0) if sq2 is not None else 0, bn, splits, ws, wsn,
-        N.pf_arg(next_weight), N.stream_ptr()), "tb_row_linear_residual")
+        N.stream_ptr()), "tb_row_linear_residual")
 
 
 def paged_attention_decode(q, out, kv_pool, *, n_q_heads, n_kv_heads, head_dim, block_size,

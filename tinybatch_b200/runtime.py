@@ -368,25 +368,25 @@ class DeviceModel:
     """Buffers and the launch sequence of the forward on one rank."""
 
     def __init__(self, weights: RankWeights, max_tokens: int = 2048, max_seqs: int = 256,
-                 comm=None, split_tokens: int | None = None, l2_prefetch_bytes: int = 0):
+                 comm=None, split_tokens: int | None = None):
         self.w = weights
         self.cfg = weights.cfg
         self.device = weights.device
         self.comm = comm
         # decode split-KV size (None: decode_split_tokens per call)
         self.split_tokens = split_tokens
-        # bytes of the next projection's weight warmed into L2 during a GEMM
-        # epilogue (0: off; on the 14B decode step it lengthened the issuing
-        # GEMM by more than it saved the next one)
-        self.l2_prefetch_bytes = l2_prefetch_bytes
         # with a communicator, sampled steps score only this rank's slice of
         # the vocabulary and exchange argmax candidates (tb_argmax_vocab_parallel);
         # full logits (sample=False) still come from the whole, replicated head
         self.vocab_parallel = comm is not None
-        # exchange sites of one forward: o_proj and down_proj of every layer,
-        # then the sampling exchange (always counted, so every forward has the
-        # same epochs whether it samples or not)
-        self.n_sites = 2 * self.cfg.n_layers + 1
+        # row-parallel exchange sites of one forward: o_proj (2l) and down_proj
+        # (2l + 1) of every layer, passed as the exchange's sequence number, so
+        # every forward starts at parity 0 and ends at parity 1
+        self.n_sites = 2 * self.cfg.n_layers
+        # when a device int64 tensor [n_sites], every row-parallel exchange
+        # raises its element to the exchange's span in ns (tp_forward's
+        # comm_stats["seconds"])
+        self.exchange_spans: torch.Tensor | None = None
         # split-K scratch (arrival counters must stay zero between calls) and
         # split-KV attention scratch live in separate arenas
         self.scratch = ops.Scratch(self.device, 1 << 20)
@@ -441,9 +441,9 @@ class DeviceModel:
             self._alloc(max(T, self.T_max), max(S, self.S_max))
 
     # one row-parallel projection: residual (+ all-reduce) + norm prologue
-    def _row(self, x, wmat, g_next, T, last: bool, md: StepMeta, site: int, plan, nxt):
+    def _row(self, x, wmat, g_next, T, last: bool, md: StepMeta, site: int, plan):
         bn, splits = plan
-        kw = dict(bn=bn, splits=splits, scratch=self.scratch, next_weight=nxt)
+        kw = dict(bn=bn, splits=splits, scratch=self.scratch)
         if last:
             kw.update(row_dst=md.row_dst, hg2=self.hg_last, sq2=self.sq_last)
         Nn, K = wmat.shape
@@ -453,9 +453,10 @@ class DeviceModel:
             self._run(f"{proj}_residual", nbytes, 2.0 * T * Nn * K, ops.row_linear_residual, x,
                       wmat, self.h[:T], g_next, self.hg[:T], self.sq, **kw)
         else:
+            span = self.exchange_spans[site] if self.exchange_spans is not None else None
             self._run(f"{proj}_allreduce_residual", nbytes, 2.0 * T * Nn * K,
                       self.comm.row_linear_residual, x, wmat, self.h[:T], g_next, self.hg[:T],
-                      self.sq, site=site, n_sites=self.n_sites, **kw)
+                      self.sq, seq=site, span=span, **kw)
         return ops.row_parts(Nn, bn, splits)
 
     def plans(self, T: int, n: int) -> dict:
@@ -481,21 +482,13 @@ class DeviceModel:
     def _world(self) -> int:
         return self.comm.world if self.comm is not None else 1
 
-    def _next(self, w: torch.Tensor, plan) -> "N.L2Prefetch | None":
-        return N.l2_next(w, plan[1], self.l2_prefetch_bytes)
-
     def forward(self, md: StepMeta, kv_pools: list[torch.Tensor], compute_logits: bool = True,
                 sample: bool = False, attn_max_ctx: int | None = None,
                 attn_split: int | None = None):
         """Launch the forward.  ``attn_max_ctx`` sizes the decode attention
         grid (default: this batch's longest context); a CUDA graph passes its
         bound so one capture serves every context length up to it, and
-        ``attn_split`` its split-KV size.
-
-        Every GEMM whose epilogue is followed by another weight-streaming GEMM
-        asks for the next weight to be warmed into L2 (o_proj -> gate/up ->
-        down -> next layer's QKV or the LM head); the QKV projection is
-        followed by attention, whose KV stream would evict such lines."""
+        ``attn_split`` its split-KV size."""
         cfg, W = self.cfg, self.w
         T, n = md.T, md.n_out
         self.ensure(T, n)
@@ -503,8 +496,6 @@ class DeviceModel:
         inv_d, eps = 1.0 / d, cfg.rms_eps
         bs = kv_pools[0].shape[3]
         pl = self.plans(T, n)
-        if self.comm is not None:
-            self.comm.begin_step()
         self._run("embed", T * d * (2 + 4 + 2), 0.0, ops.embed, md.ids, W.emb, W.layers[0].ln_in,
                   self.h[:T], self.hg[:T], self.sq[0])
         kv_row = 2 * W.n_kv * hd * 2          # K+V bytes of one token in one layer
@@ -539,22 +530,17 @@ class DeviceModel:
                     4.0 * md.pre_pairs * W.n_q * hd, ops.paged_attention_prefill,
                     self.q, self.attn, pool, block_tables=md.pre_bt, q_start=md.pre_q_start,
                     q_len=md.pre_q_len, ctx_len=md.pre_ctx, work=md.work, **akw)
-            parts = self._row(self.attn[:T], L.wo, L.ln_post, T, False, md, 2 * li, pl["o"],
-                              self._next(L.wgu, pl["gu"]))
+            parts = self._row(self.attn[:T], L.wo, L.ln_post, T, False, md, 2 * li, pl["o"])
             bn, splits = pl["gu"]
             Ngu = L.wgu.shape[0]
             self._run("gate_up_swiglu", 2 * Ngu * d + 2 * T * d + 2 * T * W.ff, 2.0 * T * Ngu * d,
                       ops.gate_up_swiglu, self.hg[:T], L.wgu, self.act[:T], n_feat=W.ff,
                       sq=self.sq[:parts], inv_d=inv_d, eps=eps, bn=bn, splits=splits,
-                      scratch=self.scratch, next_weight=self._next(L.wd, pl["down"]))
+                      scratch=self.scratch)
             last = li == len(W.layers) - 1
             g_next = W.final_norm if last else W.layers[li + 1].ln_in
-            if not last:
-                nxt = self._next(W.layers[li + 1].wqkv, pl["qkv"])
-            else:
-                nxt = self._next(W.lm_head, pl["lm"]) if compute_logits else None
             parts = self._row(self.act[:T, :W.ff], L.wd, g_next, T, last, md, 2 * li + 1,
-                              pl["down"], nxt)
+                              pl["down"])
         if not compute_logits:
             return None
         V = cfg.vocab_size
@@ -570,7 +556,7 @@ class DeviceModel:
                           sq=self.sq_last[:parts], inv_d=inv_d, eps=eps, bn=bn, splits=splits,
                           scratch=self.scratch)
             self._run("argmax", 4 * n * nv, 0.0, self.comm.argmax, self.logits[:n], nv, col0,
-                      self.next_ids[:n], site=2 * cfg.n_layers, n_sites=self.n_sites)
+                      self.next_ids[:n])
             return out
         bn, splits = pl["lm"]
         out = self.logits[:n]

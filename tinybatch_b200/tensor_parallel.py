@@ -12,7 +12,9 @@
   The two all-reduces per layer run inside the o_proj / down_proj GEMM
   epilogues over NVLink peer memory; ``comm_stats`` counts them exactly like
   the reference's wrapper (``calls`` += 1 and ``bytes`` += numel * element
-  size of the reduced ``[T, d]`` bf16 tensor per all-reduce).
+  size of the reduced ``[T, d]`` bf16 tensor per all-reduce) and adds to
+  ``seconds`` the exchange's device-measured share of each fused call (the
+  longest span any CTA spent from its first push to holding every sum).
 * ``run_tp_forward(world, w, cfg, token_ids, port)``: spawns one process per
   GPU, returns rank 0's ``(logits, stats)`` (``:138-151``), with timeouts so
   a dead rank ends the call with an error instead of a hang.
@@ -51,14 +53,19 @@ def shard_weights(w: dict, cfg: ModelConfig, rank: int, world: int) -> dict:
     return out
 
 
-_MODELS: dict = {}
+# The device model of the last weight dict tp_forward saw in this process
+# (key (id(w), world)); a new dict replaces it, so repeated calls with fresh
+# dicts do not accumulate device memory.  The entry keeps w alive, so its id
+# cannot be reused by another dict while it is cached.
+_MODEL: dict = {}
 
 
 def _rank_model(w: dict, cfg: ModelConfig, world: int):
-    """Build (once per weight dict) this rank's device model."""
+    """This rank's device model for weight dict ``w`` (built once per dict)."""
     from .model import Qwen2Paged
     key = (id(w), world)
-    if key not in _MODELS:
+    if _MODEL.get("key") != key:
+        release()
         rank = dist.get_rank() if world > 1 else 0
         comm = None
         if world > 1:
@@ -68,8 +75,19 @@ def _rank_model(w: dict, cfg: ModelConfig, world: int):
         dev = torch.device("cuda", torch.cuda.current_device())
         model = Qwen2Paged.from_weights(cfg, w, device=dev, rank=rank, world=world, comm=comm,
                                         sharded=True)
-        _MODELS[key] = (model, w)       # keeps w alive so its id stays unique
-    return _MODELS[key][0]
+        _MODEL.update(key=key, model=model, w=w)
+    return _MODEL["model"]
+
+
+def release() -> None:
+    """Drop the cached device model of ``tp_forward`` (closing its
+    communicator: every rank must call this together)."""
+    old = _MODEL.pop("model", None)
+    _MODEL.clear()
+    if old is not None and old.dm.comm is not None:
+        old.dm.comm.close()
+    del old
+    torch.cuda.empty_cache()
 
 
 @torch.inference_mode()
@@ -85,11 +103,17 @@ def tp_forward(token_ids: torch.Tensor, w: dict, cfg: ModelConfig, world: int,
     kv = m.make_kv_cache(nb, bs)
     md_all = StepMeta(ids, list(range(T)), [(0, T)], [list(range(nb))], [T], bs,
                       cfg.n_heads // cfg.n_kv_heads, m.device, all_logits=True)
-    logits = m.dm.forward(md_all, kv.pools)
-    if comm_stats is not None and world > 1:
+    timed = comm_stats is not None and world > 1
+    if timed:
+        m.dm.exchange_spans = torch.zeros(m.dm.n_sites, dtype=torch.int64, device=m.device)
+    try:
+        logits = m.dm.forward(md_all, kv.pools)
+    finally:
+        spans, m.dm.exchange_spans = m.dm.exchange_spans, None
+    if timed:
         comm_stats["calls"] += 2 * cfg.n_layers
         comm_stats["bytes"] += 2 * cfg.n_layers * T * cfg.d_model * 2
-        comm_stats.setdefault("seconds", 0.0)
+        comm_stats["seconds"] = comm_stats.get("seconds", 0.0) + float(spans.sum().item()) * 1e-9
     out = logits.clone()
     return out.cpu() if token_ids.device.type == "cpu" else out
 

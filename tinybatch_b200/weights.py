@@ -69,6 +69,38 @@ def synthetic_weights(cfg: ModelConfig, seed: int, std: float = 0.02,
     return w
 
 
+def synthetic_rank_weights(cfg: ModelConfig, seed: int, rank: int, world: int,
+                           std: float = 0.02, dtype: torch.dtype = torch.bfloat16,
+                           device: str | torch.device = "cpu",
+                           bias: bool = True) -> dict[str, torch.Tensor]:
+    """One tensor-parallel rank's slice of ``synthetic_weights(cfg, seed)``:
+    the same draw, tensor by tensor on ``device``, keeping only the rows
+    (column-parallel) or columns (row-parallel) of this rank -- the split of
+    ``shard_weights`` -- so no device or host ever holds the whole model.
+    Values equal ``shard_weights(synthetic_weights(cfg, seed, device=device),
+    cfg, rank, world)`` cast to ``dtype``."""
+    from .checkpoint import split_of
+    assert cfg.n_heads % world == 0, "q heads must divide tp degree"
+    assert cfg.n_kv_heads % world == 0, "kv heads must divide tp degree"
+    assert cfg.d_ff % world == 0, "d_ff must divide tp degree"
+    g = torch.Generator(device=device).manual_seed(seed)
+    w: dict[str, torch.Tensor] = {}
+    for name, shape, kind in weight_shapes(cfg, bias):
+        if kind == "ones":
+            full = torch.ones(shape, device=device, dtype=torch.float32)
+        else:
+            full = torch.randn(shape, generator=g, device=device, dtype=torch.float32).mul_(std)
+        dim = split_of(name)
+        if dim is not None and world > 1:
+            n = shape[dim] // world
+            full = full.narrow(dim, rank * n, n)
+        w[name] = full.to(dtype).contiguous()
+        del full
+    if cfg.tie_embeddings:
+        w["lm_head.weight"] = w["model.embed_tokens.weight"]
+    return w
+
+
 def reference_test_weights(cfg: ModelConfig, seed: int = 0) -> dict[str, torch.Tensor]:
     """The reference TP test's draw (``tests/test_tensor_parallel.py:21-45``):
     randn * 0.05, order embed, final norm, lm_head, then per layer
