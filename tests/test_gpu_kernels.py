@@ -20,6 +20,7 @@ if not torch.cuda.is_available():  # collected on CPU-only hosts, never run ther
 
 from oracle import qwen2_ref as R  # noqa: E402
 from tinybatch_b200 import _native, ops  # noqa: E402
+from tinybatch_b200.runtime import prefill_work  # noqa: E402
 
 DEV = "cuda"
 
@@ -269,8 +270,7 @@ def test_paged_attention_prefill(hq, hkv, hd, bs):
     ctx = [37, 21, 64, 200, 2]          # seq 1 and 3 have a cached prefix
     d, ref = _paged_case(hq, hkv, hd, bs, q_lens, ctx, seed=4)
     G = hq // hkv
-    work = [(i, t) for i, ql in enumerate(q_lens) for t in range((ql * G + 63) // 64)]
-    work = torch.tensor(work, dtype=torch.int32, device=DEV)
+    work = torch.tensor(prefill_work(q_lens, ctx, G), dtype=torch.int32, device=DEV)
     out = torch.zeros(sum(q_lens), hq * hd, dtype=torch.bfloat16, device=DEV)
     ops.paged_attention_prefill(d["q"], out, d["pool"], n_q_heads=hq, n_kv_heads=hkv,
                                 head_dim=hd, block_size=bs, block_tables=d["bt"],
@@ -278,6 +278,26 @@ def test_paged_attention_prefill(hq, hkv, hd, bs):
                                 work=work)
     torch.cuda.synchronize()
     torch.testing.assert_close(out.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("hq,hkv,hd,bs", [(40, 8, 128, 16), (64, 8, 128, 32), (14, 2, 64, 16)])
+def test_paged_attention_prefill_long(hq, hkv, hd, bs):
+    """Prefill over many 128-key tiles (the two-stage ring and both S buffers
+    reused several times), cached prefixes of several tiles, rows of the
+    last tile only partly valid, a one-token prompt."""
+    q_lens = [700, 129, 260, 1, 40]
+    ctx = [700, 900, 260, 513, 777]
+    d, ref = _paged_case(hq, hkv, hd, bs, q_lens, ctx, seed=9)
+    G = hq // hkv
+    work = torch.tensor(prefill_work(q_lens, ctx, G), dtype=torch.int32, device=DEV)
+    out = torch.zeros(sum(q_lens), hq * hd, dtype=torch.bfloat16, device=DEV)
+    for _ in range(2):
+        ops.paged_attention_prefill(d["q"], out, d["pool"], n_q_heads=hq, n_kv_heads=hkv,
+                                    head_dim=hd, block_size=bs, block_tables=d["bt"],
+                                    q_start=d["q_start"], q_len=d["q_len"], ctx_len=d["ctx"],
+                                    work=work)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float().cpu(), ref, atol=2e-2, rtol=2e-2)
 
 
 def test_embed_and_argmax():

@@ -114,8 +114,13 @@ def _loop_pack(token_ids, positions, slices, tables, ctx, bs, group, bt_width):
     d = subset(is_dec)
     p = subset(~is_dec)
     order = np.argsort(-d[2], kind="stable").astype(np.int32)
-    work = [(r, t) for r, ql in enumerate(p[1]) for t in range(-(-int(ql) * group // 64))]
-    work = np.asarray(work, dtype=np.int32).reshape(-1, 2)
+    # (prefill sequence, 128-row tile), most keys read first (stable)
+    tiles = []
+    for r, (ql, c) in enumerate(zip(p[1].tolist(), p[2].tolist())):
+        for t in range(-(-ql * group // 128)):
+            last = min(t * 128 + 127, ql * group - 1)
+            tiles.append((-min(c, c - ql + last // group + 1), len(tiles), r, t))
+    work = np.asarray([(r, t) for *_, r, t in sorted(tiles)], dtype=np.int32).reshape(-1, 2)
     return np.concatenate([ids, pos, slots, row_dst, d[0], d[1], d[2], d[3].ravel(), order,
                            p[0], p[1], p[2], p[3].ravel(), work.ravel()]).astype(np.int32)
 
@@ -162,3 +167,22 @@ def test_token_view_matches_list():
                 assert v[a:b] == ref[a:b], (limit, a, b)
         for k in range(-len(ref), len(ref)):
             assert v[k] == ref[k]
+
+
+def test_prefill_work_list():
+    """(sequence, 128-row tile) pairs covering every query row once, ordered
+    by the keys a tile reads (its last row's causal limit), most first."""
+    from tinybatch_b200.runtime import PREFILL_ROWS, prefill_work
+    q_len, ctx, G = [300, 5, 64, 1], [300, 900, 64, 40], 5
+    w = prefill_work(q_len, ctx, G)
+    want = sorted((r, t) for r, ql in enumerate(q_len) for t in range(-(-ql * G // PREFILL_ROWS)))
+    assert sorted(map(tuple, w.tolist())) == want
+
+    def keys(r, t):
+        last = min(t * PREFILL_ROWS + PREFILL_ROWS - 1, q_len[r] * G - 1)
+        return min(ctx[r], ctx[r] - q_len[r] + last // G + 1)
+
+    cost = [keys(r, t) for r, t in w.tolist()]
+    assert cost == sorted(cost, reverse=True)
+    assert cost[0] == 900                  # the one-row tile over a 895-token cached prefix
+    assert prefill_work([], [], G).shape == (0, 2)

@@ -24,8 +24,11 @@
 //                   TMA (a producer warp, 8-slot mbarrier ring) when the
 //                   block size is a multiple of 16 and hd is 64 or 128,
 //                   else by per-lane cp.async.
-//   prefill kernel  64 rows per CTA (16 per warp), key chunks shared by the
-//                   4 warps, causal limit per row.
+//   prefill         128 query rows per CTA (a work item (sequence, 128-row
+//                   tile) per kv head): for head_dim 64 / 128 and block sizes
+//                   that are multiples of 16 on tcgen05 (attn_prefill_tc_kernel:
+//                   TMA, S and O in TMEM); otherwise 8 warps of 16 rows on
+//                   mma.sync with key chunks shared by the warps.
 #include "attention.cuh"
 #include "common.cuh"
 #include "host.h"
@@ -525,7 +528,7 @@ __global__ void __launch_bounds__(TMA_THREADS, 3)
 constexpr int PF_STAGES = 2;
 
 template <int HD>
-__global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
   using C = ChunkLayout<HD>;
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_wait();
@@ -536,12 +539,12 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
   const int nrows_total = qlen * G;
-  const int row0 = rt * 64 + warp * 16;
+  const int row0 = rt * 128 + warp * 16;
   const int nrows = max(0, min(16, nrows_total - row0));
   const int first = ctx - qlen;
   const int* table = a.block_tables + (size_t)seq * a.bt_ld;
   // keys needed by the whole CTA: up to the last row's causal limit
-  const int last_row = min(rt * 64 + 63, nrows_total - 1);
+  const int last_row = min(rt * 128 + 127, nrows_total - 1);
   const int cta_keys = min(ctx, first + last_row / G + 1);
   const int n_chunks = (cta_keys + 15) / 16;
 
@@ -558,12 +561,12 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
   const uint32_t ring = smem_u32(smem);
   Flash<HD> f;
   f.init();
-  if (n_chunks > 0) load_chunk<HD>(a, table, kvh, ctx, 0, ring, ring + C::BYTES, threadIdx.x, 128);
+  if (n_chunks > 0) load_chunk<HD>(a, table, kvh, ctx, 0, ring, ring + C::BYTES, threadIdx.x, 256);
   cp_commit();
   for (int ci = 0; ci < n_chunks; ++ci) {
     if (ci + 1 < n_chunks) {
       const uint32_t sn = ring + ((ci + 1) % PF_STAGES) * 2 * C::BYTES;
-      load_chunk<HD>(a, table, kvh, ctx, ci + 1, sn, sn + C::BYTES, threadIdx.x, 128);
+      load_chunk<HD>(a, table, kvh, ctx, ci + 1, sn, sn + C::BYTES, threadIdx.x, 256);
     }
     cp_commit();
     cp_wait<1>();
@@ -588,6 +591,299 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const AttnArgs a) {
       *reinterpret_cast<uint32_t*>(dst + c) =
           pack_bf16x2(f.o[nt][2 * h] * inv, f.o[nt][2 * h + 1] * inv);
     }
+  }
+}
+
+// ------------------------------------------------------ prefill, tcgen05
+//
+// One CTA per (work item = (sequence, 128-row tile), kv head).  Row r of the
+// tile is query row R = 128 * tile + r: token R / G, head R % G of the kv
+// head's group.  Keys go in tiles of 128 (8 chunks of 16 tokens, each chunk
+// one block-table lookup), up to the last row's causal limit.
+//   warp 0     TMA producer: K and V of every key tile, 64-column halves, one
+//              2 KiB box per (chunk, half) straight from the pool, into a
+//              two-stage ring (mbarriers full / empty)
+//   warp 1     TMEM owner and MMA issuer: S_j = Q K_j^T (M 128, N 128 keys,
+//              K = HD) into one of two TMEM S buffers; once P_j is in shared
+//              memory, O_j = P_j V_j (M 128, N = HD, K 128 keys) into the
+//              TMEM O buffer, V read in place as an MN-major operand
+//   warps 2-5  one query row per thread (TMEM lane = row): Q into shared
+//              memory, then per key tile the row max of S_j, P_j =
+//              exp2(S_j - max) as bf16 into shared memory, the running sum,
+//              and O = O * alpha + O_{j-1} in registers (alpha: the change of
+//              the running max)
+// Shared-memory tiles use the 128-byte swizzle (rows of 64 bf16, 16-byte
+// pieces XOR-permuted by row % 8, 8-row atoms 1024 B apart), the layout TMA
+// writes and the MMA descriptors describe; Q and P are written by threads in
+// the same layout.
+constexpr int PT_ROWS = 128;    // query rows per CTA
+constexpr int PT_KEYS = 128;    // keys per tile
+constexpr int PT_THREADS = 192;
+
+template <int HD>
+struct PrefillTcLayout {
+  static constexpr int HALVES = HD / 64;                  // 64-column halves
+  static constexpr int HALF = PT_ROWS * 128;              // one [128][64] bf16 half: 16 KiB
+  static constexpr int Q_BYTES = HALVES * HALF;
+  static constexpr int KV_HALF = PT_KEYS * 128;           // [128 keys][64] bf16
+  static constexpr int STAGE = 2 * HALVES * KV_HALF;      // K then V
+  static constexpr int P_BYTES = 2 * HALF;                // [128 rows][128 keys] bf16
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = Q_BYTES;
+  static constexpr int OFF_P = OFF_KV + 2 * STAGE;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int SMEM = OFF_BAR + 16 * 8 + 1024;     // barriers + alignment slack
+  static constexpr uint32_t TMEM_COLS = 512;              // S0, S1, O
+  static constexpr uint32_t COL_S0 = 0, COL_S1 = PT_KEYS, COL_O = 2 * PT_KEYS;
+  static_assert(COL_O + HD <= TMEM_COLS, "TMEM: two S buffers and O");
+  static_assert(SMEM <= 232448, "prefill shared memory above 227 KiB");
+};
+
+// Byte offset of 16-byte piece c (0..7) of row r in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(PT_THREADS, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const AttnArgs a) {
+  using L = PrefillTcLayout<HD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;        // [2]
+  uint64_t* kv_empty = bars + 2;   // [2]
+  uint64_t* s_full = bars + 4;     // [2]
+  uint64_t* s_free = bars + 6;     // [2]
+  uint64_t* p_full = bars + 8;
+  uint64_t* o_full = bars + 9;
+  uint64_t* q_full = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // step metadata comes from host copies, not from the previous kernel
+  const int seq = a.work[2 * blockIdx.x], rt = a.work[2 * blockIdx.x + 1];
+  const int kvh = blockIdx.y;
+  const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
+  const int G = a.n_q_heads / a.n_kv_heads;
+  const int nrows_total = qlen * G;
+  const int first = ctx - qlen;
+  const int last_row = min(rt * PT_ROWS + PT_ROWS - 1, nrows_total - 1);
+  const int keys = max(1, min(ctx, first + last_row / G + 1));   // keys this CTA needs
+  const int n_tiles = (keys + PT_KEYS - 1) / PT_KEYS;
+  const int* table = a.block_tables + (size_t)seq * a.bt_ld;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(q_full, 128);
+    fence_mbar_init();
+    prefetch_tmap(&pool_map);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) pdl_trigger();
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      pdl_wait();   // the pool is written by the previous kernel
+      const int last_chunk = (keys - 1) / 16;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&kv_full[st], L::STAGE);
+        uint8_t* kst = smem + L::OFF_KV + st * L::STAGE;
+        uint8_t* vst = kst + L::HALVES * L::KV_HALF;
+#pragma unroll 1
+        for (int c = 0; c < PT_KEYS / 16; ++c) {
+          // chunks past the keys this CTA needs repeat its last chunk (masked)
+          const int chunk = min(j * (PT_KEYS / 16) + c, last_chunk);
+          const int key0 = chunk * 16;
+          int blk = table[key0 / a.block_size];
+          if (blk < 0 || blk >= a.num_blocks) {
+            set_status(ERR_BAD_INDEX);
+            blk = 0;
+          }
+          const int row_k = (int)(((size_t)blk * 2 * a.n_kv_heads + kvh) * a.block_size +
+                                  key0 % a.block_size);
+          const int row_v = row_k + a.n_kv_heads * a.block_size;
+#pragma unroll
+          for (int h = 0; h < L::HALVES; ++h) {
+            tma_load_2d(kst + h * L::KV_HALF + c * 2048, &pool_map, &kv_full[st], h * 64, row_k);
+            tma_load_2d(vst + h * L::KV_HALF + c * 2048, &pool_map, &kv_full[st], h * 64, row_v);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_m128(PT_KEYS);
+      constexpr uint32_t idesc_o = idesc_bf16_m128(HD) | (1u << 16);   // B (V) MN-major
+      const uint32_t qbase = sbase + L::OFF_Q, pbase = sbase + L::OFF_P;
+      bool ok = mbar_wait(q_full, 0);
+      tc_fence_after();
+      auto issue_pv = [&](int t) {
+        if (!mbar_wait(p_full, t & 1)) ok = false;
+        tc_fence_after();
+        const uint32_t vbase = sbase + L::OFF_KV + (t & 1) * L::STAGE + L::HALVES * L::KV_HALF;
+#pragma unroll
+        for (int ks = 0; ks < PT_KEYS / 16; ++ks) {
+          const uint64_t ad = sw128_desc(pbase + (ks >> 2) * L::HALF + (ks & 3) * 32);
+          const uint64_t bd = sw128_mn_desc(vbase + ks * 2048, L::KV_HALF, 1024);
+          tc_mma_bf16(tmem + L::COL_O, ad, bd, idesc_o, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(o_full);
+        tc_commit(&kv_empty[t & 1]);
+      };
+      int issued = 0;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) break;
+        if (j >= 2 && !mbar_wait(&s_free[st], ((j >> 1) - 1) & 1)) break;
+        tc_fence_after();
+        const uint32_t kbase = sbase + L::OFF_KV + st * L::STAGE;
+#pragma unroll
+        for (int h = 0; h < L::HALVES; ++h)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_bf16(tmem + (st ? L::COL_S1 : L::COL_S0),
+                        sw128_desc(qbase + h * L::HALF + kk * 32),
+                        sw128_desc(kbase + h * L::KV_HALF + kk * 32), idesc_s,
+                        (h | kk) ? 1u : 0u);
+        tc_commit(&s_full[st]);
+        issued = j + 1;
+        if (j >= 1) issue_pv(j - 1);
+      }
+      if (ok && issued == n_tiles) issue_pv(n_tiles - 1);
+    }
+  } else {
+    // ---------------- softmax: one query row per thread
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;                 // TMEM lane of this thread
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int R = rt * PT_ROWS + r;
+    const bool valid = R < nrows_total;
+    const int limit = valid ? first + R / G : -1;   // last key this row sees
+    pdl_wait();   // q is written by the previous kernel
+    {
+      uint8_t* qs = smem + L::OFF_Q;
+      const __nv_bfloat16* src =
+          a.q + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_q + (size_t)(kvh * G + R % G) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (valid) v = *reinterpret_cast<const uint4*>(src + c * 8);
+        *reinterpret_cast<uint4*>(qs + (c >> 3) * L::HALF + sw128_off(r, c & 7)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(q_full);
+    }
+    float o[HD];
+#pragma unroll
+    for (int c = 0; c < HD; ++c) o[c] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    uint8_t* ps = smem + L::OFF_P;
+    const float sc = a.scale_log2;
+    auto add_o = [&](int t, float alpha) {
+      if (!mbar_wait(o_full, t & 1)) return;
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + L::COL_O + c0 + lane_off, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[c0 + e] = o[c0 + e] * alpha + v[e];
+      }
+    };
+    int done = 0;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1)) break;
+      tc_fence_after();
+      const uint32_t ts = tmem + (st ? L::COL_S1 : L::COL_S0) + lane_off;
+      const int k0 = j * PT_KEYS;
+      // row max over this tile's visible keys
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < PT_KEYS; c0 += 32) {
+        float v[32];
+        tmem_ld32(ts + c0, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (k0 + c0 + e <= limit) mx = fmaxf(mx, v[e] * sc);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float mu = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = exp2f(m - mu);
+      // the previous tile's P V is complete: fold it in (this also frees P)
+      if (j >= 1) add_o(j - 1, alpha_prev);
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < PT_KEYS; c0 += 32) {
+        float v[32];
+        tmem_ld32(ts + c0, v);
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = k0 + c0 + e <= limit ? exp2f(v[e] * sc - mu) : 0.f;
+          const float p1 = k0 + c0 + e + 1 <= limit ? exp2f(v[e + 1] * sc - mu) : 0.f;
+          sum += p0 + p1;
+          w[e >> 1] = pack_bf16x2(p0, p1);
+        }
+        // 32 keys = 4 pieces of 16 bytes in the half of key c0 / 64
+        uint8_t* half = ps + (c0 >> 6) * L::HALF;
+        const int c8 = (c0 & 63) >> 3;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<uint4*>(half + sw128_off(r, c8 + k)) =
+              make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);        // S buffer st may be overwritten
+      l = l * alpha + sum;
+      m = m_new;
+      alpha_prev = alpha;
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);             // P_j is in shared memory
+      done = j + 1;
+    }
+    if (done == n_tiles) add_o(n_tiles - 1, alpha_prev);
+    if (valid) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst =
+          a.out + (size_t)(q0 + R / G) * a.ld_out + (size_t)(kvh * G + R % G) * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 8) {
+        uint4 u;
+        u.x = pack_bf16x2(o[c] * inv, o[c + 1] * inv);
+        u.y = pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
+        u.z = pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv);
+        u.w = pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv);
+        *reinterpret_cast<uint4*>(dst + c) = u;
+      }
+    }
+  }
+  if (warp == 1) pdl_wait();   // every CTA waits before it exits (PDL chain)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
   }
 }
 
@@ -627,8 +923,24 @@ static int decode_launch(const AttnArgs& a, cudaStream_t st) {
 template <int HD>
 static int prefill_launch(const AttnArgs& a, int n_work, cudaStream_t st) {
   const int smem = PF_STAGES * 2 * ChunkLayout<HD>::BYTES;
-  return launch_pdl(attn_prefill_kernel<HD>, dim3(n_work, a.n_kv_heads), dim3(128), smem, st, 1,
+  return launch_pdl(attn_prefill_kernel<HD>, dim3(n_work, a.n_kv_heads), dim3(256), smem, st, 1,
                     "attention prefill launch", a);
+}
+
+template <int HD>
+static int prefill_tc_launch(const AttnArgs& a, int n_work, cudaStream_t st) {
+  using L = PrefillTcLayout<HD>;
+  static std::atomic<unsigned long long> attr_devs{0};
+  if (int rc = smem_attr_once(attn_prefill_tc_kernel<HD>, L::SMEM, attr_devs,
+                              "prefill smem attribute"))
+    return rc;
+  CUtensorMap map;
+  const uint64_t rows = (uint64_t)a.num_blocks * 2 * a.n_kv_heads * a.block_size;
+  if (rows >= (1ull << 31)) return arg_err("KV pool rows beyond 2^31");
+  int rc = make_tmap_2d(&map, a.pool, HD, rows, (uint64_t)HD * 2, 64, 16);
+  if (rc) return rc;
+  return launch_pdl(attn_prefill_tc_kernel<HD>, dim3(n_work, a.n_kv_heads), dim3(PT_THREADS),
+                    L::SMEM, st, 1, "attention prefill launch", map, a);
 }
 
 static int check_common(const AttnArgs& a, int head_dim) {
@@ -662,10 +974,12 @@ int attn_prefill(AttnArgs a, int head_dim, int n_work, cudaStream_t st) {
   if (rc) return rc;
   if (n_work == 0) return TB_OK;
   a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  // TMA boxes need 16-token chunks inside one block and a 16-byte aligned pool
+  const bool tc = a.block_size % 16 == 0 && reinterpret_cast<uintptr_t>(a.pool) % 16 == 0;
   switch (head_dim) {
     case 16: return prefill_launch<16>(a, n_work, st);
-    case 64: return prefill_launch<64>(a, n_work, st);
-    default: return prefill_launch<128>(a, n_work, st);
+    case 64: return tc ? prefill_tc_launch<64>(a, n_work, st) : prefill_launch<64>(a, n_work, st);
+    default: return tc ? prefill_tc_launch<128>(a, n_work, st) : prefill_launch<128>(a, n_work, st);
   }
 }
 

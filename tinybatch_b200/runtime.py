@@ -238,6 +238,25 @@ def rope_tables(cfg: ModelConfig, device) -> tuple[torch.Tensor, torch.Tensor]:
 
 # ------------------------------------------------------------------ metadata
 
+PREFILL_ROWS = 128      # query rows per prefill attention work item
+
+
+def prefill_work(q_len, ctx, group: int) -> np.ndarray:
+    """Prefill attention work list: (sequence, tile of 128 query rows) pairs,
+    row = token * group + head, ordered by the keys each tile reads (its last
+    row's causal limit), most first, so long tiles start early."""
+    items, cost = [], []
+    for r, (ql, c) in enumerate(zip(np.asarray(q_len).tolist(), np.asarray(ctx).tolist())):
+        rows = ql * group
+        first = c - ql
+        for t in range(-(-rows // PREFILL_ROWS)):
+            last = min(t * PREFILL_ROWS + PREFILL_ROWS - 1, rows - 1)
+            items.append((r, t))
+            cost.append(min(c, first + last // group + 1))
+    order = sorted(range(len(items)), key=lambda i: -cost[i])
+    return np.asarray([items[i] for i in order], dtype=np.int32).reshape(-1, 2)
+
+
 class StepMeta:
     """Device int32 metadata of one flat mixed batch, built on the host with
     numpy and shipped in one host->device copy.  Block tables may be lists
@@ -247,7 +266,7 @@ class StepMeta:
     sequence's last token, else -1); for the decode subset (q_len*G <= 16)
     and the prefill subset: q_start, q_len, ctx_len [n], block tables
     [n, bt_ld] (-1 padded); the decode subset's order by descending context
-    length; the prefill (sequence, 64-row tile) work list."""
+    length; the prefill (sequence, 128-row tile) work list (``prefill_work``)."""
 
     def __init__(self, token_ids, positions, seq_slices, block_tables, context_lens,
                  block_size: int, group: int, device, pinned: bool = True,
@@ -315,8 +334,7 @@ class StepMeta:
 
         d_idx, d_qs, d_ql, d_ctx, d_bt = subset(is_dec)
         p_idx, p_qs, p_ql, p_ctx, p_bt = subset(~is_dec)
-        work = [(r, t) for r, ql in enumerate(p_ql) for t in range(-(-int(ql) * group // 64))]
-        work = np.asarray(work, dtype=np.int32).reshape(-1, 2)
+        work = prefill_work(p_ql, p_ctx, group)
         # decode sequences longest first: the attention grid dispatches in this order
         d_order = np.argsort(-d_ctx, kind="stable").astype(np.int32)
         parts = [ids, pos, slots, row_dst, d_qs, d_ql, d_ctx, d_bt.ravel(), d_order, p_qs, p_ql,
