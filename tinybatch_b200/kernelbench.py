@@ -2,6 +2,7 @@
 the small case the ncu captures run on.
 
     python -m tinybatch_b200.kernelbench [--tp T] [--layers L] [--reps R]
+    python -m tinybatch_b200.kernelbench --prefill N [--prompt-len P] [--cached C]
 
 Workload: the Qwen2.5-14B layer shapes (d 5120, 40 q / 8 kv heads, hd 128,
 ff 13824, vocab 152064) cut to ``L`` decoder layers (default 1) and sharded
@@ -23,6 +24,14 @@ and TFLOP/s, and the fraction of the roofline
 
 with the burst figures of MEASURED_PEAKS.json (a copy and a cuBLAS GEMM
 measured on this pool's B200s).
+
+``--prefill N``: one prefill forward of N prompts instead (lengths drawn from
+the 14B benchmark's U[128, 2048] with its seed, or all ``--prompt-len`` P);
+with ``--cached C`` every prompt continues a C-token prefix already in the
+pool (the 72B workload's shared 1024-token prefix), so attention reads C + P
+keys for the P new tokens.  Prompt tokens/s of the forward and, for
+attention, causal (query, key) pairs x 4 flops per head dim against the bf16
+tensor rate.
 """
 from __future__ import annotations
 
@@ -137,6 +146,77 @@ def run(tp: int = 1, layers: int = 1, reps: int = 5,
     return rows
 
 
+def run_prefill(n: int, prompt_len: int | None, cached: int, tp: int = 1, layers: int = 1,
+                reps: int = 3) -> list[dict]:
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rng = random.Random(SEED)
+    lens = [prompt_len or rng.randint(128, 2048) for _ in range(n)]
+    T = sum(lens)
+    cfg = named_config("qwen2.5-14b", n_layers=layers)
+    w = synthetic_weights(cfg, SEED, dtype=torch.bfloat16, device=dev)
+    model = Qwen2Paged.from_weights(cfg, w, device=dev, rank=0, world=tp, comm=None,
+                                    max_tokens=T, max_seqs=n)
+    del w
+    torch.cuda.empty_cache()
+    tables, nb = [], 0
+    for L in lens:
+        k = -(-(cached + L) // BLOCK)
+        tables.append(list(range(nb, nb + k)))
+        nb += k
+    cache = model.make_kv_cache(nb, BLOCK)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    for pool in cache.pools:
+        pool.copy_(torch.randn(pool.shape, generator=g, device=dev).mul_(0.5))
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=torch.Generator().manual_seed(SEED))
+    pos, slices, s0 = [], [], 0
+    for L in lens:
+        pos += list(range(cached, cached + L))
+        slices.append((s0, s0 + L))
+        s0 += L
+    md = model.metadata(ids.tolist(), pos, slices, tables, [cached + L for L in lens], BLOCK)
+    model.forward_meta(md, cache)
+    torch.cuda.synchronize()
+    _native.raise_on_status("kernelbench prefill warm-up")
+    times: dict[str, list[float]] = {}
+    meta: dict[str, tuple[int, float, float]] = {}
+    fwd = []
+    for _ in range(reps):
+        torch.cuda._sleep(50_000_000)
+        model.dm.prof = []
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        model.forward_meta(md, cache)
+        e1.record()
+        torch.cuda.synchronize()
+        fwd.append(e0.elapsed_time(e1) * 1e3)
+        per: dict[str, list] = {}
+        for kind, s, e, nbytes, flops in model.dm.prof:
+            per.setdefault(kind, []).append((s.elapsed_time(e) * 1e3, nbytes, flops))
+        for kind, lst in per.items():
+            times.setdefault(kind, []).append(sum(t for t, _, _ in lst) / len(lst))
+            meta[kind] = (len(lst), sum(b for _, b, _ in lst) / len(lst),
+                          sum(f for _, _, f in lst) / len(lst))
+        model.dm.prof = None
+    _native.raise_on_status("kernelbench prefill")
+    pk, src = peaks()
+    us_fwd = statistics.median(fwd)
+    rows = [{"kernel": "prefill_forward", "tp": tp, "layers": layers, "prompts": n,
+             "prompt_tokens": T, "cached_prefix": cached, "us": round(us_fwd, 1),
+             "prompt_tokens_per_s": round(T / us_fwd * 1e6, 1)}]
+    for kind, ts in times.items():
+        n_l, nbytes, flops = meta[kind]
+        us = statistics.median(ts)
+        t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
+        t_tc = flops / (pk["bf16_tflops"] * 1e12)
+        rows.append({"kernel": kind, "tp": tp, "launches_per_step": n_l,
+                     "us_per_launch": round(us, 2), "TFLOPs": round(flops / us / 1e6, 1),
+                     "GBps": round(nbytes / us / 1e3, 1),
+                     "bound": "hbm" if t_hbm >= t_tc else "tensor",
+                     "frac": round(max(t_hbm, t_tc) * 1e6 / us, 3), "peaks": src})
+    rows.sort(key=lambda r: -r.get("us_per_launch", 0) * r.get("launches_per_step", 0))
+    return rows
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tp", type=int, default=1, help="shard as rank 0 of this many ranks")
@@ -144,7 +224,15 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--split-tokens", default=None,
                     help="decode split-KV size (default: the runtime's policy); comma list")
+    ap.add_argument("--prefill", type=int, default=0, help="prefill N prompts instead")
+    ap.add_argument("--prompt-len", type=int, default=None)
+    ap.add_argument("--cached", type=int, default=0)
     args = ap.parse_args()
+    if args.prefill:
+        for r in run_prefill(args.prefill, args.prompt_len, args.cached, args.tp, args.layers,
+                             args.reps):
+            print(json.dumps(r), flush=True)
+        return
     splits = [None] if args.split_tokens is None else [int(v) or None for v in
                                                        args.split_tokens.split(",")]
     for st in splits:
