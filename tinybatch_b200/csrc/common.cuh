@@ -155,11 +155,8 @@ __device__ __forceinline__ unsigned long long ld_word(const void* p) {
 // Bounded poll of one 16-byte packet: returns once neither word is the
 // sentinel (false, with ERR_PEER_TIMEOUT recorded, when the budget runs out).
 // t0: the caller's start time of this wait (0 = not started yet).
-// Polls back off (32 ns doubling to 256 ns between loads), so thousands of
-// waiting threads do not keep the L2 busy that the peers' stores land in.
 __device__ __forceinline__ bool poll_pkt(const void* p, unsigned long long& a,
                                          unsigned long long& b, uint64_t& t0) {
-  uint32_t ns = 32;
   for (uint32_t i = 0; a == TB_SENTINEL || b == TB_SENTINEL; ++i) {
     if ((i & 255u) == 0) {
       const uint64_t now = globaltimer_ns();
@@ -169,8 +166,6 @@ __device__ __forceinline__ bool poll_pkt(const void* p, unsigned long long& a,
         return false;
       }
     }
-    __nanosleep(ns);
-    if (ns < 256) ns <<= 1;
     ld_pkt(p, a, b);
   }
   return true;
