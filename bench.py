@@ -118,7 +118,7 @@ def peaks() -> tuple[dict, str]:
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 25 ms) of this GPU while the timed regions run."""
+    """nvidia-smi samples (every 100 ms) of this GPU while the timed regions run."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -133,7 +133,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "25"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             time.sleep(0.3)       # first sample before the timed region starts
         except OSError:
@@ -685,8 +685,10 @@ def run_workload(args, wl, cfg, rank, world, local, dev, model, prompts, outs, g
                         max_running=n_req, max_model_len=4096, max_new_tokens=max(outs),
                         device=str(dev), overlap_steps=not wl["prefix"])
 
+    eng = LLMEngine(ecfg, model=model)
+
     def one_run():
-        eng = LLMEngine(ecfg, model=model)
+        eng.reset()          # cold block manager and scheduler; pool and graphs kept
         torch.cuda.synchronize()
         barrier(world)
         t0 = time.perf_counter()
@@ -700,8 +702,7 @@ def run_workload(args, wl, cfg, rank, world, local, dev, model, prompts, outs, g
         wall = reduce_over_ranks(time.perf_counter() - t0, world)
         return eng, reqs, wall, steps
 
-    for _ in range(max(1, min(args.warmup, 1))):   # warm-up run: graphs, kernel attributes
-        one_run()
+    one_run()            # warm-up run: captures the decode graph of every batch size
     with ClockSampler(local) as clocks:
         eng, reqs, wall, steps = one_run()
     gen = sum(len(r.output_token_ids) for r in reqs)

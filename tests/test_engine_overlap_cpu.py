@@ -232,3 +232,18 @@ def test_stop_token_keeps_the_reference_block_tables():
             for pool in eng.kv_cache.pools:
                 assert pool[blk, 0, 0, off, 0].item() == r.req_id
                 assert pool[blk, 0, 0, off, 1].item() == pos
+
+
+def test_reset_starts_cold():
+    """reset() forgets every request and the prefix cache, keeping the pool
+    and graphs: the next identical workload gets identical tables."""
+    eng = _engine(prefix=True)
+    eng._graphs[1] = _Graph()
+    reqs = _running(eng, [[5] * 9, [5] * 9], [4, 4])
+    first = [list(r.block_table) for r in reqs]
+    assert eng.block_manager.prefix_hits > 0          # the second prompt hit the first
+    eng.reset()
+    assert not eng.scheduler.has_work() and eng.block_manager.prefix_hits == 0
+    assert eng.block_manager.num_free() == 64 and eng._graphs
+    again = [list(r.block_table) for r in _running(eng, [[5] * 9, [5] * 9], [4, 4])]
+    assert again == first

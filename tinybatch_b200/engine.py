@@ -109,6 +109,15 @@ class LLMEngine:
 
     # ------------------------------------------------------------- API
 
+    def reset(self) -> None:
+        """Forget every request: a fresh block manager and scheduler over
+        the same KV pool, model and captured decode graphs (which depend on
+        neither), so a new workload starts cold without re-capturing."""
+        self.drain()
+        self.block_manager = BlockManager(self.cfg.num_blocks, self.cfg.block_size,
+                                          self.cfg.enable_prefix_caching)
+        self.scheduler = Scheduler(self.cfg, self.block_manager)
+
     def add_request_ids(self, ids: list[int], max_new_tokens: int | None = None,
                         temperature: float | None = None, top_p: float | None = None) -> Request:
         ids = list(ids)[: self.cfg.max_model_len - 1]
