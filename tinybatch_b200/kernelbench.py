@@ -3,6 +3,7 @@ the small case the ncu captures run on.
 
     python -m tinybatch_b200.kernelbench [--tp T] [--layers L] [--reps R]
     python -m tinybatch_b200.kernelbench --prefill N [--prompt-len P] [--cached C]
+    python -m tinybatch_b200.kernelbench --plan qkv=256x5,o=128x2 ...   (override the planner)
 
 Workload: the Qwen2.5-14B layer shapes (d 5120, 40 q / 8 kv heads, hd 128,
 ff 13824, vocab 152064) cut to ``L`` decoder layers (default 1) and sharded
@@ -92,11 +93,31 @@ def build(tp: int, layers: int, device: torch.device):
     return cfg, model, cache, md
 
 
+def parse_plan(text: str | None) -> dict:
+    """'qkv=256x5,o=128x2' -> {'qkv': (256, 5), 'o': (128, 2)} (tile width x
+    split-K factor per projection: qkv, o, gu, down, lm)."""
+    out = {}
+    for item in (text or "").split(","):
+        if item:
+            k, v = item.split("=")
+            bn, sp = v.split("x")
+            out[k] = (int(bn), int(sp))
+    return out
+
+
 def run(tp: int = 1, layers: int = 1, reps: int = 5,
-        split_tokens: int | None = None) -> list[dict]:
+        split_tokens: int | None = None, plan: dict | None = None) -> list[dict]:
     dev = torch.device("cuda", torch.cuda.current_device())
     cfg, model, cache, md = build(tp, layers, dev)
     model.dm.split_tokens = split_tokens
+    if plan:
+        planner = model.dm.plans
+
+        def plans(T, n):
+            p = planner(T, n)
+            p.update(plan)
+            return p
+        model.dm.plans = plans
     for _ in range(2):
         model.forward_meta(md, cache, sample=True)
     torch.cuda.synchronize()
@@ -129,6 +150,7 @@ def run(tp: int = 1, layers: int = 1, reps: int = 5,
     _native.raise_on_status("kernelbench")
     pk, src = peaks()
     rows = [{"kernel": "forward", "tp": tp, "layers": layers,
+             "plans": {k: list(v) for k, v in model.dm.plans(N_SEQ, N_SEQ).items()},
              "split_tokens": split_tokens or "auto", "launches_per_step": 1,
              "us_per_launch": round(statistics.median(fwd), 2)}]
     for kind, ts in times.items():
@@ -224,6 +246,8 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--split-tokens", default=None,
                     help="decode split-KV size (default: the runtime's policy); comma list")
+    ap.add_argument("--plan", default=None,
+                    help="override GEMM plans, e.g. qkv=256x5,o=128x2 (tile width x splits)")
     ap.add_argument("--prefill", type=int, default=0, help="prefill N prompts instead")
     ap.add_argument("--prompt-len", type=int, default=None)
     ap.add_argument("--cached", type=int, default=0)
@@ -236,7 +260,7 @@ def main() -> None:
     splits = [None] if args.split_tokens is None else [int(v) or None for v in
                                                        args.split_tokens.split(",")]
     for st in splits:
-        for r in run(args.tp, args.layers, args.reps, st):
+        for r in run(args.tp, args.layers, args.reps, st, parse_plan(args.plan)):
             print(json.dumps(r), flush=True)
 
 
