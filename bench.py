@@ -297,7 +297,7 @@ def run_reference(args) -> None:
         "extrapolated_ms_per_decode_step": 1e3 * (cfg.n_layers * layer_s + head_s),
         "extrapolated_from": f"1 full-width layer x{cfg.n_layers} + LM head (timed on 1/8 of "
                              "the vocabulary, x8)",
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": f"{wl['model']} decode, {len(prompts)} requests, TP=1 on host "
                                "cores, contexts of the GPU arm's timed steps"},
@@ -646,7 +646,7 @@ def run_steady(args, wl, cfg, rank, world, local, dev, model, prompts, gate) -> 
         line = {
             "metric": "decode_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights, random prompt ids)",
             "config": {"workload": f"{wl['model']} decode, {n_req} requests, prompts "
                                    f"U[{wl['prompt'][0]},{wl['prompt'][1]}], {out_tokens} output "
@@ -712,7 +712,7 @@ def run_workload(args, wl, cfg, rank, world, local, dev, model, prompts, outs, g
         line = {
             "metric": "generated_tokens_per_s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": 1e3 * wall / steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights, random prompt ids)",
             "config": {"workload": f"{wl['model']}, {n_req} requests at once, continuous batching, "
                                    f"prefix caching {'on' if wl['prefix'] else 'off'}, TP={world}",
