@@ -511,6 +511,20 @@ def _cpu_leg(args, cfg, ctx, rank, world):
     return line
 
 
+def prefill_flops(cfg, prompt_lens: list[int]) -> float:
+    """Algorithmic flop of prefilling the prompts with no cached prefix: the
+    projections (2 x tokens x weights per layer), causal attention
+    (4 x head_dim x q heads x visible query-key pairs per layer) and the LM
+    head on each prompt's last token."""
+    hd, d = cfg.head_dim, cfg.d_model
+    per_tok = 2 * (d * (cfg.n_heads + 2 * cfg.n_kv_heads) * hd + cfg.n_heads * hd * d
+                   + 3 * d * cfg.d_ff)
+    tokens = sum(prompt_lens)
+    pairs = sum(p * (p + 1) // 2 for p in prompt_lens)
+    return float(cfg.n_layers * (per_tok * tokens + 4 * hd * cfg.n_heads * pairs)
+                 + 2 * cfg.vocab_size * d * len(prompt_lens))
+
+
 def run_steady(args, wl, cfg, rank, world, local, dev, model, prompts, gate) -> None:
     from tinybatch_b200.config import EngineConfig
     from tinybatch_b200.engine import LLMEngine
@@ -643,6 +657,8 @@ def run_steady(args, wl, cfg, rank, world, local, dev, model, prompts, gate) -> 
     ctx = decode_contexts(prompts, args.warmup, args.steps)
     cpu = _cpu_leg(args, cfg, ctx, rank, world)
     if rank == 0:
+        pf_flops = prefill_flops(cfg, [len(p) for p in prompts])
+        pf_peak = pk["bf16_tflops_sustained"] * world
         line = {
             "metric": "decode_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
@@ -666,6 +682,14 @@ def run_steady(args, wl, cfg, rank, world, local, dev, model, prompts, gate) -> 
                             for kk, vv in k.items()} for n, k in kinds.items()},
             "clocks": clocks.summary(),
             "parity": gate,
+            "prefill": {"prompts": n_req, "prompt_tokens": prompt_tokens,
+                        "steps": prefill_steps, "wall_s": round(prefill_s, 3),
+                        "tokens_per_s": round(prompt_tokens / prefill_s, 1),
+                        "flop": pf_flops, "tflops": round(pf_flops / prefill_s / 1e12, 1),
+                        "peak_tflops": pf_peak, "peak": f"bf16 sustained x {world} ({src})",
+                        "frac": round(pf_flops / prefill_s / 1e12 / pf_peak, 3),
+                        "timing": "host wall clock over the engine's prefill steps "
+                                  "(scheduling and metadata included)"},
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
