@@ -601,17 +601,24 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
 // head's group.  Keys go in tiles of 128 (8 chunks of 16 tokens, each chunk
 // one block-table lookup), up to the last row's causal limit.
 //   warp 0     TMA producer: K and V of every key tile, 64-column halves, one
-//              2 KiB box per (chunk, half) straight from the pool, into a
-//              two-stage ring (mbarriers full / empty)
+//              2 KiB box per (chunk, half) straight from the pool, into
+//              two-stage rings with separate K and V barriers (a K stage is
+//              refilled as soon as its S MMA is done, a V stage once its PV
+//              MMA is done)
 //   warp 1     TMEM owner and MMA issuer: S_j = Q K_j^T (M 128, N 128 keys,
 //              K = HD) into one of two TMEM S buffers; once P_j is in shared
-//              memory, O_j = P_j V_j (M 128, N = HD, K 128 keys) into the
-//              TMEM O buffer, V read in place as an MN-major operand
+//              memory, O += P_j V_j (M 128, N = HD, K 128 keys) into the TMEM
+//              O accumulator, V read in place as an MN-major operand
 //   warps 2-5  one query row per thread (TMEM lane = row): Q into shared
-//              memory, then per key tile the row max of S_j, P_j =
-//              exp2(S_j - max) as bf16 into shared memory, the running sum,
-//              and O = O * alpha + O_{j-1} in registers (alpha: the change of
-//              the running max)
+//              memory, then per key tile S_j into registers (the S buffer is
+//              released at once), the row max, P_j = exp2(S_j - ref) as bf16
+//              into one of two shared-memory P buffers, and the running sum
+// O stays in TMEM across the key tiles.  A row's exponent reference `ref`
+// moves only when its running max exceeds it by more than PT_RESCALE (log2
+// units): then the row's O is rescaled in TMEM (after the PV MMAs issued so
+// far complete) and its sum by the same factor.  Otherwise P and O carry a
+// factor of at most 2^PT_RESCALE, which the final division by the sum
+// removes; bf16 rounding of P is relative, so the factor costs no precision.
 // Shared-memory tiles use the 128-byte swizzle (rows of 64 bf16, 16-byte
 // pieces XOR-permuted by row % 8, 8-row atoms 1024 B apart), the layout TMA
 // writes and the MMA descriptors describe; Q and P are written by threads in
@@ -619,6 +626,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
 constexpr int PT_ROWS = 128;    // query rows per CTA
 constexpr int PT_KEYS = 128;    // keys per tile
 constexpr int PT_THREADS = 192;
+constexpr float PT_RESCALE = 8.f;
 
 template <int HD>
 struct PrefillTcLayout {
@@ -626,16 +634,19 @@ struct PrefillTcLayout {
   static constexpr int HALF = PT_ROWS * 128;              // one [128][64] bf16 half: 16 KiB
   static constexpr int Q_BYTES = HALVES * HALF;
   static constexpr int KV_HALF = PT_KEYS * 128;           // [128 keys][64] bf16
-  static constexpr int STAGE = 2 * HALVES * KV_HALF;      // K then V
+  static constexpr int KV_PART = HALVES * KV_HALF;        // K (or V) of one key tile
+  static constexpr int STAGE = 2 * KV_PART;               // K then V
   static constexpr int P_BYTES = 2 * HALF;                // [128 rows][128 keys] bf16
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = Q_BYTES;
-  static constexpr int OFF_P = OFF_KV + 2 * STAGE;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  static constexpr int SMEM = OFF_BAR + 16 * 8 + 1024;     // barriers + alignment slack
+  static constexpr int OFF_P = OFF_KV + 2 * STAGE;        // two P buffers
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int N_BARS = 18;
+  static constexpr int SMEM = OFF_BAR + 24 * 8 + 1024;     // barriers + TMEM slot + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;              // S0, S1, O
   static constexpr uint32_t COL_S0 = 0, COL_S1 = PT_KEYS, COL_O = 2 * PT_KEYS;
   static_assert(COL_O + HD <= TMEM_COLS, "TMEM: two S buffers and O");
+  static_assert(N_BARS * 8 + 4 <= 24 * 8, "barrier area");
   static_assert(SMEM <= 232448, "prefill shared memory above 227 KiB");
 };
 
@@ -651,14 +662,17 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* kv_full = bars;        // [2]
-  uint64_t* kv_empty = bars + 2;   // [2]
-  uint64_t* s_full = bars + 4;     // [2]
-  uint64_t* s_free = bars + 6;     // [2]
-  uint64_t* p_full = bars + 8;
-  uint64_t* o_full = bars + 9;
-  uint64_t* q_full = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* k_full = bars;         // [2]
+  uint64_t* k_empty = bars + 2;    // [2]
+  uint64_t* v_full = bars + 4;     // [2]
+  uint64_t* v_empty = bars + 6;    // [2]
+  uint64_t* s_full = bars + 8;     // [2]
+  uint64_t* s_free = bars + 10;    // [2]
+  uint64_t* p_full = bars + 12;    // [2]
+  uint64_t* pv_done = bars + 14;   // [2]
+  uint64_t* q_full = bars + 16;
+  uint64_t* mma_idle = bars + 17;  // every MMA of the CTA complete (before TMEM is freed)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // step metadata comes from host copies, not from the previous kernel
@@ -675,14 +689,17 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_full, 1);
     mbar_init(q_full, 128);
+    mbar_init(mma_idle, 1);
     fence_mbar_init();
     prefetch_tmap(&pool_map);
   }
@@ -702,13 +719,14 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     if (lane == 0) {
       pdl_wait();   // the pool is written by the previous kernel
       const int last_chunk = (keys - 1) / 16;
+      int nk = 0, nv = 0;   // key tiles whose K / V loads were issued
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&kv_full[st], L::STAGE);
+        const uint32_t ph = ((j >> 1) - 1) & 1;
         uint8_t* kst = smem + L::OFF_KV + st * L::STAGE;
-        uint8_t* vst = kst + L::HALVES * L::KV_HALF;
-#pragma unroll 1
+        uint8_t* vst = kst + L::KV_PART;
+        int row_k[PT_KEYS / 16];
+#pragma unroll
         for (int c = 0; c < PT_KEYS / 16; ++c) {
           // chunks past the keys this CTA needs repeat its last chunk (masked)
           const int chunk = min(j * (PT_KEYS / 16) + c, last_chunk);
@@ -718,42 +736,61 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
             set_status(ERR_BAD_INDEX);
             blk = 0;
           }
-          const int row_k = (int)(((size_t)blk * 2 * a.n_kv_heads + kvh) * a.block_size +
-                                  key0 % a.block_size);
-          const int row_v = row_k + a.n_kv_heads * a.block_size;
-#pragma unroll
-          for (int h = 0; h < L::HALVES; ++h) {
-            tma_load_2d(kst + h * L::KV_HALF + c * 2048, &pool_map, &kv_full[st], h * 64, row_k);
-            tma_load_2d(vst + h * L::KV_HALF + c * 2048, &pool_map, &kv_full[st], h * 64, row_v);
-          }
+          row_k[c] = (int)(((size_t)blk * 2 * a.n_kv_heads + kvh) * a.block_size +
+                           key0 % a.block_size);
         }
+        if (j >= 2 && !mbar_wait(&k_empty[st], ph)) break;
+        mbar_arrive_expect_tx(&k_full[st], L::KV_PART);
+#pragma unroll
+        for (int c = 0; c < PT_KEYS / 16; ++c)
+#pragma unroll
+          for (int h = 0; h < L::HALVES; ++h)
+            tma_load_2d(kst + h * L::KV_HALF + c * 2048, &pool_map, &k_full[st], h * 64, row_k[c]);
+        nk = j + 1;
+        if (j >= 2 && !mbar_wait(&v_empty[st], ph)) break;
+        mbar_arrive_expect_tx(&v_full[st], L::KV_PART);
+#pragma unroll
+        for (int c = 0; c < PT_KEYS / 16; ++c)
+#pragma unroll
+          for (int h = 0; h < L::HALVES; ++h)
+            tma_load_2d(vst + h * L::KV_HALF + c * 2048, &pool_map, &v_full[st], h * 64,
+                        row_k[c] + a.n_kv_heads * a.block_size);
+        nv = j + 1;
       }
+      // a consumer that gave up leaves loads in flight: let them land before exit
+      for (int t = max(0, nk - 2); t < nk; ++t) mbar_wait(&k_full[t & 1], (t >> 1) & 1);
+      for (int t = max(0, nv - 2); t < nv; ++t) mbar_wait(&v_full[t & 1], (t >> 1) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_m128(PT_KEYS);
       constexpr uint32_t idesc_o = idesc_bf16_m128(HD) | (1u << 16);   // B (V) MN-major
-      const uint32_t qbase = sbase + L::OFF_Q, pbase = sbase + L::OFF_P;
+      const uint32_t qbase = sbase + L::OFF_Q;
       bool ok = mbar_wait(q_full, 0);
       tc_fence_after();
       auto issue_pv = [&](int t) {
-        if (!mbar_wait(p_full, t & 1)) ok = false;
+        const int b = t & 1;
+        if (!mbar_wait(&v_full[b], (t >> 1) & 1) || !mbar_wait(&p_full[b], (t >> 1) & 1)) {
+          ok = false;
+          return;
+        }
         tc_fence_after();
-        const uint32_t vbase = sbase + L::OFF_KV + (t & 1) * L::STAGE + L::HALVES * L::KV_HALF;
+        const uint32_t vbase = sbase + L::OFF_KV + b * L::STAGE + L::KV_PART;
+        const uint32_t pbase = sbase + L::OFF_P + b * L::P_BYTES;
 #pragma unroll
         for (int ks = 0; ks < PT_KEYS / 16; ++ks) {
           const uint64_t ad = sw128_desc(pbase + (ks >> 2) * L::HALF + (ks & 3) * 32);
           const uint64_t bd = sw128_mn_desc(vbase + ks * 2048, L::KV_HALF, 1024);
-          tc_mma_bf16(tmem + L::COL_O, ad, bd, idesc_o, ks > 0 ? 1u : 0u);
+          tc_mma_bf16(tmem + L::COL_O, ad, bd, idesc_o, (t > 0 || ks > 0) ? 1u : 0u);
         }
-        tc_commit(o_full);
-        tc_commit(&kv_empty[t & 1]);
+        tc_commit(&v_empty[b]);
+        tc_commit(&pv_done[b]);
       };
       int issued = 0;
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) break;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) break;
         if (j >= 2 && !mbar_wait(&s_free[st], ((j >> 1) - 1) & 1)) break;
         tc_fence_after();
         const uint32_t kbase = sbase + L::OFF_KV + st * L::STAGE;
@@ -765,11 +802,14 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
                         sw128_desc(qbase + h * L::HALF + kk * 32),
                         sw128_desc(kbase + h * L::KV_HALF + kk * 32), idesc_s,
                         (h | kk) ? 1u : 0u);
+        tc_commit(&k_empty[st]);
         tc_commit(&s_full[st]);
         issued = j + 1;
         if (j >= 1) issue_pv(j - 1);
       }
       if (ok && issued == n_tiles) issue_pv(n_tiles - 1);
+      tc_commit(mma_idle);
+      mbar_wait(mma_idle, 0);
     }
   } else {
     // ---------------- softmax: one query row per thread
@@ -793,88 +833,104 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(q_full);
     }
-    float o[HD];
-#pragma unroll
-    for (int c = 0; c < HD; ++c) o[c] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    uint8_t* ps = smem + L::OFF_P;
+    const uint32_t to = tmem + L::COL_O + lane_off;
+    float ref = -INFINITY, l = 0.f;   // exponent reference (log2 units) and running sum
     const float sc = a.scale_log2;
-    auto add_o = [&](int t, float alpha) {
-      if (!mbar_wait(o_full, t & 1)) return;
-      tc_fence_after();
-#pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + L::COL_O + c0 + lane_off, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[c0 + e] = o[c0 + e] * alpha + v[e];
-      }
-    };
     int done = 0;
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1)) break;
+      // waits are made warp-uniform: the TMEM accesses below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1))) break;
       tc_fence_after();
-      const uint32_t ts = tmem + (st ? L::COL_S1 : L::COL_S0) + lane_off;
-      const int k0 = j * PT_KEYS;
-      // row max over this tile's visible keys
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < PT_KEYS; c0 += 32) {
-        float v[32];
-        tmem_ld32(ts + c0, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (k0 + c0 + e <= limit) mx = fmaxf(mx, v[e] * sc);
+      float s[PT_KEYS];
+      {
+        const uint32_t ts = tmem + (st ? L::COL_S1 : L::COL_S0) + lane_off;
+        tmem_ld64(ts, s);
+        tmem_ld64(ts + 64, s + 64);
       }
-      const float m_new = fmaxf(m, mx);
-      const float mu = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m - mu);
-      // the previous tile's P V is complete: fold it in (this also frees P)
-      if (j >= 1) add_o(j - 1, alpha_prev);
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);        // S buffer st may be overwritten
+      const int k0 = j * PT_KEYS;
+      if (k0 + PT_KEYS - 1 > limit) {  // the causal edge (or an empty row)
+#pragma unroll
+        for (int e = 0; e < PT_KEYS; ++e)
+          if (k0 + e > limit) s[e] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < PT_KEYS; ++e) mx = fmaxf(mx, s[e]);
+      mx *= sc;
+      const bool move = mx > ref + PT_RESCALE;   // any finite max when ref is -inf
+      const bool rescale = move && ref != -INFINITY;
+      const float alpha = rescale ? ex2_approx(ref - mx) : 1.f;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O holds PV_0 .. PV_{j-1}: once the last of them is complete, scale
+        // the warp's rows in place (alpha = 1 for rows that keep their ref)
+        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)))
+          break;
+        tc_fence_after();
+#pragma unroll
+        for (int c0 = 0; c0 < HD; c0 += 32) {
+          float v[32];
+          tmem_ld32(to + c0, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] *= alpha;
+          tmem_st32(to + c0, v);
+        }
+        tmem_wait_st();
+      }
+      if (move) ref = mx;
+      l *= alpha;
+      const float mu = ref == -INFINITY ? 0.f : ref;
+      // P buffer st is free once PV_{j-2} has completed
+      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[st], ((j >> 1) - 1) & 1))) break;
+      uint8_t* pb = smem + L::OFF_P + st * L::P_BYTES;
       float sum = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int c0 = 0; c0 < PT_KEYS; c0 += 32) {
-        float v[32];
-        tmem_ld32(ts + c0, v);
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = k0 + c0 + e <= limit ? exp2f(v[e] * sc - mu) : 0.f;
-          const float p1 = k0 + c0 + e + 1 <= limit ? exp2f(v[e + 1] * sc - mu) : 0.f;
+          const float p0 = ex2_approx(fmaf(s[c0 + e], sc, -mu));
+          const float p1 = ex2_approx(fmaf(s[c0 + e + 1], sc, -mu));
           sum += p0 + p1;
           w[e >> 1] = pack_bf16x2(p0, p1);
         }
         // 32 keys = 4 pieces of 16 bytes in the half of key c0 / 64
-        uint8_t* half = ps + (c0 >> 6) * L::HALF;
+        uint8_t* half = pb + (c0 >> 6) * L::HALF;
         const int c8 = (c0 & 63) >> 3;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           *reinterpret_cast<uint4*>(half + sw128_off(r, c8 + k)) =
               make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[st]);        // S buffer st may be overwritten
-      l = l * alpha + sum;
-      m = m_new;
-      alpha_prev = alpha;
+      l += sum;
+      tc_fence_before();               // the rescale's TMEM stores precede PV_j
       fence_proxy_async_smem();
-      mbar_arrive(p_full);             // P_j is in shared memory
+      mbar_arrive(&p_full[st]);        // P_j is in shared memory
       done = j + 1;
     }
-    if (done == n_tiles) add_o(n_tiles - 1, alpha_prev);
-    if (valid) {
+    if (done == n_tiles &&
+        __all_sync(0xffffffffu, mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1))) {
+      tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* dst =
-          a.out + (size_t)(q0 + R / G) * a.ld_out + (size_t)(kvh * G + R % G) * HD;
+          a.out + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_out + (size_t)(kvh * G + R % G) * HD;
 #pragma unroll
-      for (int c = 0; c < HD; c += 8) {
-        uint4 u;
-        u.x = pack_bf16x2(o[c] * inv, o[c + 1] * inv);
-        u.y = pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv);
-        u.z = pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv);
-        u.w = pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + c) = u;
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float v[32];
+        tmem_ld32(to + c0, v);   // warp-collective: every lane loads
+        if (valid) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 u;
+            u.x = pack_bf16x2(v[c] * inv, v[c + 1] * inv);
+            u.y = pack_bf16x2(v[c + 2] * inv, v[c + 3] * inv);
+            u.z = pack_bf16x2(v[c + 4] * inv, v[c + 5] * inv);
+            u.w = pack_bf16x2(v[c + 6] * inv, v[c + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + c0 + c) = u;
+          }
+        }
       }
     }
   }
@@ -886,8 +942,6 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     tmem_dealloc(tmem, L::TMEM_COLS);
   }
 }
-
-// ------------------------------------------------------------------ host side
 
 template <int HD>
 static int decode_tma_launch(const AttnArgs& a, cudaStream_t st) {
