@@ -52,8 +52,15 @@ const char* tb_last_error(void);
  * to the peer ranks, 4 owned sums sent (two-shot), 5 every value of the
  * all-reduce received, 6 end, 7 split-K
  * chunks stored to their cluster owners, 8 every cluster member's chunks
- * arrived (unreached points are left as they were).  buf must hold 16 entries per CTA of the largest
- * launch.  Not thread-safe; NULL turns it off. */
+ * arrived (unreached points are left as they were).  The tcgen05 prefill
+ * attention (CTA c = work item + n_work * kv head) writes 32 entries per CTA
+ * at buf[32*c + k]: %globaltimer at k = 0 (start) and 31 (end), and clock64
+ * stamps (SM cycles; 30 / 29 = start / end) of its pipeline: 1 Q stored, 26 Q seen
+ * by the MMA thread, 27 output read, and for key tiles j < 3 at 2 + 8j: K
+ * loads start / issued, V loads start / issued, S issued, S read, P stored,
+ * PV issued.  buf must hold 16
+ * entries per CTA of the largest GEMM launch and 32 per CTA of the largest
+ * prefill.  Not thread-safe; NULL turns it off. */
 int tb_debug_trace(unsigned long long* buf);
 
 /* Read (and optionally clear) the device status word of the current device.

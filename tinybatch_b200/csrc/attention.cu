@@ -35,6 +35,7 @@
 
 namespace tb {
 
+extern unsigned long long* g_debug_trace;   // tb_debug_trace (null: no timeline)
 
 
 __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
@@ -63,6 +64,12 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool p
                : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// One arrival on `bar` once every cp.async this thread issued so far has
+// landed (the barrier's count includes the arrival).
+__device__ __forceinline__ void cp_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
 template <int N>
 __device__ __forceinline__ void cp_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
@@ -527,6 +534,17 @@ __global__ void __launch_bounds__(TMA_THREADS, 3)
 
 constexpr int PF_STAGES = 2;
 
+// A prefill work item (sequence, 128-row tile) that names a sequence of the
+// call, a row tile inside its prompt, a prompt no longer than its context and
+// a context its block-table row can hold.
+__device__ __forceinline__ bool prefill_item_ok(const AttnArgs& a, int seq, int rt) {
+  if (seq < 0 || seq >= a.n_seqs || rt < 0) return false;
+  const int ctx = a.ctx_len[seq], qlen = a.q_len[seq];
+  const int G = a.n_q_heads / a.n_kv_heads;
+  return qlen >= 1 && qlen <= ctx && rt * 128 < qlen * G &&
+         (ctx + a.block_size - 1) / a.block_size <= a.bt_ld;
+}
+
 template <int HD>
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
   using C = ChunkLayout<HD>;
@@ -536,6 +554,10 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
   const int seq = a.work[2 * blockIdx.x], rt = a.work[2 * blockIdx.x + 1];
   const int kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (!prefill_item_ok(a, seq, rt)) {
+    if (threadIdx.x == 0) set_status(ERR_BAD_INDEX);
+    return;
+  }
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
   const int nrows_total = qlen * G;
@@ -600,33 +622,66 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
 // tile is query row R = 128 * tile + r: token R / G, head R % G of the kv
 // head's group.  Keys go in tiles of 128 (8 chunks of 16 tokens, each chunk
 // one block-table lookup), up to the last row's causal limit.
-//   warp 0     TMA producer: K and V of every key tile, 64-column halves, one
-//              2 KiB box per (chunk, half) straight from the pool, into
-//              two-stage rings with separate K and V barriers (a K stage is
-//              refilled as soon as its S MMA is done, a V stage once its PV
-//              MMA is done)
+//   warps 0/10 loaders of K / V: every key tile gathered from the pool
+//              through the block table with 16-byte cp.async pieces (a warp
+//              instruction moves two whole 256-byte key rows), written in the
+//              128-byte-swizzled layout the MMA descriptors describe, into
+//              two-stage rings (a K stage is refilled as soon as its S MMA is
+//              done, a V stage once its PV MMA is done).  A tile's barrier
+//              completes when its pieces have landed (cp.async arrivals), and
+//              the MMA thread fences them over to the async proxy.  (TMA boxes of one 16-token block half -- 2 KiB,
+//              all the pool keeps contiguous at block size 16 -- issued at
+//              ~40 ns each from one thread, left the tensor pipe waiting.)
 //   warp 1     TMEM owner and MMA issuer: S_j = Q K_j^T (M 128, N 128 keys,
-//              K = HD) into one of two TMEM S buffers; once P_j is in shared
-//              memory, O += P_j V_j (M 128, N = HD, K 128 keys) into the TMEM
-//              O accumulator, V read in place as an MN-major operand
-//   warps 2-5  one query row per thread (TMEM lane = row): Q into shared
-//              memory, then per key tile S_j into registers (the S buffer is
-//              released at once), the row max, P_j = exp2(S_j - ref) as bf16
-//              into one of two shared-memory P buffers, and the running sum
+//              K = HD) into one of two TMEM S buffers, two tiles ahead of the
+//              softmax; once P_j is in shared memory, O += P_j V_j (M 128,
+//              N = HD, K 128 keys) into the TMEM O accumulator, V read in
+//              place as an MN-major operand
+//   warps 2-9  two threads per query row (TMEM lane = row; warps w and w + 4
+//              share a lane quarter): Q into shared memory, then per key tile
+//              the row max over all 128 scores (each thread reads both
+//              halves), and for its own half of the keys P_j = exp2(S_j -
+//              ref) as bf16 into one of two shared-memory P buffers and its
+//              part of the running sum
 // O stays in TMEM across the key tiles.  A row's exponent reference `ref`
 // moves only when its running max exceeds it by more than PT_RESCALE (log2
 // units): then the row's O is rescaled in TMEM (after the PV MMAs issued so
-// far complete) and its sum by the same factor.  Otherwise P and O carry a
-// factor of at most 2^PT_RESCALE, which the final division by the sum
-// removes; bf16 rounding of P is relative, so the factor costs no precision.
+// far complete; each of its two threads scales half the columns) and its
+// sums by the same factor.  Otherwise P and O carry a factor of at most
+// 2^PT_RESCALE, which the final division by the sum removes; bf16 rounding
+// of P is relative, so the factor costs no precision.  Both threads of a row
+// see the same scores and take the same decisions.
 // Shared-memory tiles use the 128-byte swizzle (rows of 64 bf16, 16-byte
 // pieces XOR-permuted by row % 8, 8-row atoms 1024 B apart), the layout TMA
 // writes and the MMA descriptors describe; Q and P are written by threads in
 // the same layout.
-constexpr int PT_ROWS = 128;    // query rows per CTA
-constexpr int PT_KEYS = 128;    // keys per tile
-constexpr int PT_THREADS = 192;
+constexpr int PT_ROWS = 128;     // query rows per CTA
+constexpr int PT_KEYS = 128;     // keys per tile
+constexpr int PT_THREADS = 352;  // K loader, MMA, 8 softmax warps, V loader
+constexpr int PT_SOFT = 256;     // softmax threads
 constexpr float PT_RESCALE = 8.f;
+
+// Debug timeline of a prefill CTA (tb_debug_trace), PT_TR_POINTS slots:
+// 0 / 31 %globaltimer at the first softmax thread's start / end, 30 its
+// clock64 at start (29: at end); the other slots are clock64 stamps (SM
+// cycles): 1 Q stored, 26 the MMA thread sees Q, 27 the output is read from
+// TMEM, and for key tiles k < 3 at 2 + 8k: +0 / +1 K_k loads start / issued,
+// +2 / +3 V_k loads start / issued (loaders; start = its stage is free),
+// +4 S_k issued (MMA), +5 S_k in registers, +6 P_k stored (softmax), +7 PV_k
+// issued (MMA).
+enum : int { PT_TR_Q = 1, PT_TR_TILES = 3, PT_TR_QSEEN = 26, PT_TR_OREAD = 27, PT_TR_CLK1 = 29,
+             PT_TR_CLK0 = 30, PT_TR_END = 31, PT_TR_POINTS = 32 };
+
+__device__ __forceinline__ void pt_put(const AttnArgs& a, int point, unsigned long long v) {
+  if (a.trace != nullptr)
+    a.trace[(size_t)(blockIdx.x + blockIdx.y * gridDim.x) * PT_TR_POINTS + point] = v;
+}
+__device__ __forceinline__ void pt_clk(const AttnArgs& a, int point) {
+  if (a.trace != nullptr) pt_put(a, point, (unsigned long long)clock64());
+}
+__device__ __forceinline__ void pt_tile(const AttnArgs& a, int k, int what) {
+  if (a.trace != nullptr && k < PT_TR_TILES) pt_clk(a, 2 + 8 * k + what);
+}
 
 template <int HD>
 struct PrefillTcLayout {
@@ -641,12 +696,13 @@ struct PrefillTcLayout {
   static constexpr int OFF_KV = Q_BYTES;
   static constexpr int OFF_P = OFF_KV + 2 * STAGE;        // two P buffers
   static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-  static constexpr int N_BARS = 18;
+  static constexpr int N_BARS = 19;
   static constexpr int SMEM = OFF_BAR + 24 * 8 + 1024;     // barriers + TMEM slot + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;              // S0, S1, O
   static constexpr uint32_t COL_S0 = 0, COL_S1 = PT_KEYS, COL_O = 2 * PT_KEYS;
   static_assert(COL_O + HD <= TMEM_COLS, "TMEM: two S buffers and O");
   static_assert(N_BARS * 8 + 4 <= 24 * 8, "barrier area");
+  static_assert(2 * PT_ROWS * 4 <= Q_BYTES, "the final sum exchange reuses the Q tile");
   static_assert(SMEM <= 232448, "prefill shared memory above 227 KiB");
 };
 
@@ -657,7 +713,7 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 
 template <int HD>
 __global__ void __launch_bounds__(PT_THREADS, 1)
-    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const AttnArgs a) {
+    attn_prefill_tc_kernel(const AttnArgs a) {
   using L = PrefillTcLayout<HD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
@@ -672,12 +728,19 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   uint64_t* pv_done = bars + 14;   // [2]
   uint64_t* q_full = bars + 16;
   uint64_t* mma_idle = bars + 17;  // every MMA of the CTA complete (before TMEM is freed)
+  uint64_t* l_ready = bars + 18;   // both partial sums of every row stored
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // step metadata comes from host copies, not from the previous kernel
   const int seq = a.work[2 * blockIdx.x], rt = a.work[2 * blockIdx.x + 1];
   const int kvh = blockIdx.y;
+  if (!prefill_item_ok(a, seq, rt)) {   // uniform over the CTA: nothing set up yet
+    if (threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) set_status(ERR_BAD_INDEX);
+    return;
+  }
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
   const int nrows_total = qlen * G;
@@ -689,19 +752,19 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
+      mbar_init(&k_full[i], 32);
       mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
+      mbar_init(&v_full[i], 32);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&s_free[i], PT_SOFT);
+      mbar_init(&p_full[i], PT_SOFT);
       mbar_init(&pv_done[i], 1);
     }
-    mbar_init(q_full, 128);
+    mbar_init(q_full, PT_SOFT);
     mbar_init(mma_idle, 1);
+    mbar_init(l_ready, PT_SOFT);
     fence_mbar_init();
-    prefetch_tmap(&pool_map);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, L::TMEM_COLS);
@@ -714,53 +777,57 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   if (threadIdx.x == 0) pdl_trigger();
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == 0) {
-    // ---------------- TMA producer
-    if (lane == 0) {
-      pdl_wait();   // the pool is written by the previous kernel
-      const int last_chunk = (keys - 1) / 16;
-      int nk = 0, nv = 0;   // key tiles whose K / V loads were issued
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = ((j >> 1) - 1) & 1;
-        uint8_t* kst = smem + L::OFF_KV + st * L::STAGE;
-        uint8_t* vst = kst + L::KV_PART;
-        int row_k[PT_KEYS / 16];
-#pragma unroll
-        for (int c = 0; c < PT_KEYS / 16; ++c) {
-          // chunks past the keys this CTA needs repeat its last chunk (masked)
-          const int chunk = min(j * (PT_KEYS / 16) + c, last_chunk);
-          const int key0 = chunk * 16;
-          int blk = table[key0 / a.block_size];
-          if (blk < 0 || blk >= a.num_blocks) {
-            set_status(ERR_BAD_INDEX);
-            blk = 0;
-          }
-          row_k[c] = (int)(((size_t)blk * 2 * a.n_kv_heads + kvh) * a.block_size +
-                           key0 % a.block_size);
-        }
-        if (j >= 2 && !mbar_wait(&k_empty[st], ph)) break;
-        mbar_arrive_expect_tx(&k_full[st], L::KV_PART);
-#pragma unroll
-        for (int c = 0; c < PT_KEYS / 16; ++c)
-#pragma unroll
-          for (int h = 0; h < L::HALVES; ++h)
-            tma_load_2d(kst + h * L::KV_HALF + c * 2048, &pool_map, &k_full[st], h * 64, row_k[c]);
-        nk = j + 1;
-        if (j >= 2 && !mbar_wait(&v_empty[st], ph)) break;
-        mbar_arrive_expect_tx(&v_full[st], L::KV_PART);
-#pragma unroll
-        for (int c = 0; c < PT_KEYS / 16; ++c)
-#pragma unroll
-          for (int h = 0; h < L::HALVES; ++h)
-            tma_load_2d(vst + h * L::KV_HALF + c * 2048, &pool_map, &v_full[st], h * 64,
-                        row_k[c] + a.n_kv_heads * a.block_size);
-        nv = j + 1;
+  if (warp == 0 || warp == PT_THREADS / 32 - 1) {
+    // ---------------- loaders: K (warp 0) and V (the last warp)
+    const int is_v = warp != 0;
+    uint64_t* full = is_v ? v_full : k_full;
+    uint64_t* empty = is_v ? v_empty : k_empty;
+    const int last_chunk = (keys - 1) / 16;
+    constexpr int PPK = HD / 8;                      // 16-byte pieces per key row
+    constexpr int KEYS_PER_INSN = 32 / PPK;          // key rows one warp instruction moves
+    // lane c < 8: the block-table entry of chunk c of the tile (chunks past
+    // the CTA's last one repeat it: their keys are masked), one tile ahead
+    auto entry = [&](int j) {
+      return lane < PT_KEYS / 16 ? table[min(j * (PT_KEYS / 16) + lane, last_chunk) * 16 /
+                                         a.block_size]
+                                 : 0;
+    };
+    int blk = entry(0);
+    pdl_wait();   // the pool is written by the previous kernel
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j & 1;
+      const int blk_next = j + 1 < n_tiles ? entry(j + 1) : 0;
+      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&empty[st], ((j >> 1) - 1) & 1))) break;
+      if (lane == 0) pt_tile(a, j, 2 * is_v);
+      // lane c: first pool row of chunk c
+      int b = blk;
+      if (lane < PT_KEYS / 16 && (b < 0 || b >= a.num_blocks)) {
+        set_status(ERR_BAD_INDEX);
+        b = 0;
       }
-      // a consumer that gave up leaves loads in flight: let them land before exit
-      for (int t = max(0, nk - 2); t < nk; ++t) mbar_wait(&k_full[t & 1], (t >> 1) & 1);
-      for (int t = max(0, nv - 2); t < nv; ++t) mbar_wait(&v_full[t & 1], (t >> 1) & 1);
+      const int key0 = min(j * (PT_KEYS / 16) + lane, last_chunk) * 16;
+      const int rk = (int)(((size_t)b * 2 * a.n_kv_heads + (size_t)is_v * a.n_kv_heads + kvh) *
+                               a.block_size + key0 % a.block_size);
+      const uint32_t stage = sbase + L::OFF_KV + st * L::STAGE + is_v * L::KV_PART;
+#pragma unroll 1
+      for (int c = 0; c < PT_KEYS / 16; ++c) {
+        const int row0 = __shfl_sync(0xffffffffu, rk, c);
+#pragma unroll
+        for (int i = 0; i < 16 / KEYS_PER_INSN; ++i) {
+          const int kk = i * KEYS_PER_INSN + lane / PPK;   // key within the chunk
+          const int pc = lane % PPK, h = pc >> 3, pw = pc & 7;
+          const int key = c * 16 + kk;                      // key within the tile
+          const __nv_bfloat16* src = a.pool + (size_t)(row0 + kk) * HD + pc * 8;
+          cp_async16(stage + h * L::KV_HALF + key * 128 + ((pw ^ (key & 7)) << 4), src, true);
+        }
+      }
+      // the stage's barrier completes once every lane's pieces have landed;
+      // the MMA thread makes them visible to the tensor core (proxy fence)
+      cp_arrive_noinc(&full[st]);
+      if (lane == 0) pt_tile(a, j, 2 * is_v + 1);
+      blk = blk_next;
     }
+    cp_wait<0>();   // nothing in flight at exit
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
@@ -769,30 +836,13 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       const uint32_t qbase = sbase + L::OFF_Q;
       bool ok = mbar_wait(q_full, 0);
       tc_fence_after();
-      auto issue_pv = [&](int t) {
-        const int b = t & 1;
-        if (!mbar_wait(&v_full[b], (t >> 1) & 1) || !mbar_wait(&p_full[b], (t >> 1) & 1)) {
-          ok = false;
-          return;
-        }
-        tc_fence_after();
-        const uint32_t vbase = sbase + L::OFF_KV + b * L::STAGE + L::KV_PART;
-        const uint32_t pbase = sbase + L::OFF_P + b * L::P_BYTES;
-#pragma unroll
-        for (int ks = 0; ks < PT_KEYS / 16; ++ks) {
-          const uint64_t ad = sw128_desc(pbase + (ks >> 2) * L::HALF + (ks & 3) * 32);
-          const uint64_t bd = sw128_mn_desc(vbase + ks * 2048, L::KV_HALF, 1024);
-          tc_mma_bf16(tmem + L::COL_O, ad, bd, idesc_o, (t > 0 || ks > 0) ? 1u : 0u);
-        }
-        tc_commit(&v_empty[b]);
-        tc_commit(&pv_done[b]);
-      };
-      int issued = 0;
-      for (int j = 0; j < n_tiles && ok; ++j) {
+      pt_clk(a, PT_TR_QSEEN);
+      auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) break;
-        if (j >= 2 && !mbar_wait(&s_free[st], ((j >> 1) - 1) & 1)) break;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        if (j >= 2 && !mbar_wait(&s_free[st], ((j >> 1) - 1) & 1)) return false;
         tc_fence_after();
+        fence_proxy_async_smem();   // K arrived through cp.async (generic proxy)
         const uint32_t kbase = sbase + L::OFF_KV + st * L::STAGE;
 #pragma unroll
         for (int h = 0; h < L::HALVES; ++h)
@@ -804,37 +854,74 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
                         (h | kk) ? 1u : 0u);
         tc_commit(&k_empty[st]);
         tc_commit(&s_full[st]);
-        issued = j + 1;
-        if (j >= 1) issue_pv(j - 1);
+        pt_tile(a, j, 4);
+        return true;
+      };
+      auto issue_pv = [&](int t) -> bool {
+        const int b = t & 1;
+        if (!mbar_wait(&v_full[b], (t >> 1) & 1) || !mbar_wait(&p_full[b], (t >> 1) & 1))
+          return false;
+        tc_fence_after();
+        fence_proxy_async_smem();   // V arrived through cp.async (generic proxy)
+        const uint32_t vbase = sbase + L::OFF_KV + b * L::STAGE + L::KV_PART;
+        const uint32_t pbase = sbase + L::OFF_P + b * L::P_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < PT_KEYS / 16; ++ks) {
+          const uint64_t ad = sw128_desc(pbase + (ks >> 2) * L::HALF + (ks & 3) * 32);
+          const uint64_t bd = sw128_mn_desc(vbase + ks * 2048, L::KV_HALF, 1024);
+          tc_mma_bf16(tmem + L::COL_O, ad, bd, idesc_o, (t > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc_commit(&v_empty[b]);
+        tc_commit(&pv_done[b]);
+        pt_tile(a, t, 7);
+        return true;
+      };
+      // S runs two tiles ahead of the softmax; PV_t goes out as soon as P_t is in
+      for (int j = 0; j < 2 && j < n_tiles && ok; ++j) ok = issue_s(j);
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        ok = issue_pv(t);
+        if (ok && t + 2 < n_tiles) ok = issue_s(t + 2);
       }
-      if (ok && issued == n_tiles) issue_pv(n_tiles - 1);
       tc_commit(mma_idle);
       mbar_wait(mma_idle, 0);
     }
   } else {
-    // ---------------- softmax: one query row per thread
+    // ---------------- softmax: two threads per query row
     const int q4 = warp & 3;
+    const int hh = (warp - 2) >> 2;               // which half of the keys (and of O)
     const int r = q4 * 32 + lane;                 // TMEM lane of this thread
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const int R = rt * PT_ROWS + r;
     const bool valid = R < nrows_total;
     const int limit = valid ? first + R / G : -1;   // last key this row sees
+    const bool tracer = threadIdx.x == 64;
+    if (tracer && a.trace != nullptr) {
+      pt_put(a, 0, globaltimer_ns());
+      pt_clk(a, PT_TR_CLK0);
+    }
     pdl_wait();   // q is written by the previous kernel
     {
       uint8_t* qs = smem + L::OFF_Q;
       const __nv_bfloat16* src =
           a.q + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_q + (size_t)(kvh * G + R % G) * HD;
+      uint4 v[HD / 16];
 #pragma unroll
-      for (int c = 0; c < HD / 8; ++c) {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (valid) v = *reinterpret_cast<const uint4*>(src + c * 8);
-        *reinterpret_cast<uint4*>(qs + (c >> 3) * L::HALF + sw128_off(r, c & 7)) = v;
+      for (int i = 0; i < HD / 16; ++i) {
+        const int c = hh * (HD / 16) + i;
+        v[i] = valid ? *reinterpret_cast<const uint4*>(src + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int i = 0; i < HD / 16; ++i) {
+        const int c = hh * (HD / 16) + i;
+        *reinterpret_cast<uint4*>(qs + (c >> 3) * L::HALF + sw128_off(r, c & 7)) = v[i];
       }
       fence_proxy_async_smem();
       mbar_arrive(q_full);
+      if (tracer) pt_clk(a, PT_TR_Q);
     }
-    const uint32_t to = tmem + L::COL_O + lane_off;
-    float ref = -INFINITY, l = 0.f;   // exponent reference (log2 units) and running sum
+    constexpr int OH = HD / 2;                    // O columns of this thread
+    const uint32_t to = tmem + L::COL_O + (uint32_t)(hh * OH) + lane_off;
+    float ref = -INFINITY, l = 0.f;   // exponent reference (log2 units) and this half's sum
     const float sc = a.scale_log2;
     int done = 0;
     for (int j = 0; j < n_tiles; ++j) {
@@ -842,35 +929,46 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       // waits are made warp-uniform: the TMEM accesses below are warp-collective
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1))) break;
       tc_fence_after();
-      float s[PT_KEYS];
+      const int k0 = j * PT_KEYS;
+      const uint32_t ts = tmem + (st ? L::COL_S1 : L::COL_S0) + lane_off;
+      float s[64];
+      float mx = -INFINITY;
+      tmem_ld64(ts + hh * 64, s);
       {
-        const uint32_t ts = tmem + (st ? L::COL_S1 : L::COL_S0) + lane_off;
-        tmem_ld64(ts, s);
-        tmem_ld64(ts + 64, s + 64);
+        // the other half's scores, for the row max only
+        const int ko = k0 + (1 - hh) * 64;
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 32) {
+          float o[32];
+          tmem_ld32(ts + (1 - hh) * 64 + c0, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, ko + c0 + e <= limit ? o[e] : -INFINITY);
+        }
       }
       tc_fence_before();
       mbar_arrive(&s_free[st]);        // S buffer st may be overwritten
-      const int k0 = j * PT_KEYS;
-      if (k0 + PT_KEYS - 1 > limit) {  // the causal edge (or an empty row)
+      if (tracer) pt_tile(a, j, 5);
+      const int ks = k0 + hh * 64;
+      if (ks + 63 > limit) {           // the causal edge (or an empty row)
 #pragma unroll
-        for (int e = 0; e < PT_KEYS; ++e)
-          if (k0 + e > limit) s[e] = -INFINITY;
+        for (int e = 0; e < 64; ++e)
+          if (ks + e > limit) s[e] = -INFINITY;
       }
-      float mx = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < PT_KEYS; ++e) mx = fmaxf(mx, s[e]);
+      for (int e = 0; e < 64; ++e) mx = fmaxf(mx, s[e]);
       mx *= sc;
       const bool move = mx > ref + PT_RESCALE;   // any finite max when ref is -inf
       const bool rescale = move && ref != -INFINITY;
       const float alpha = rescale ? ex2_approx(ref - mx) : 1.f;
       if (__any_sync(0xffffffffu, rescale)) {
         // O holds PV_0 .. PV_{j-1}: once the last of them is complete, scale
-        // the warp's rows in place (alpha = 1 for rows that keep their ref)
+        // this thread's half of its row in place (alpha = 1 for rows that
+        // keep their ref)
         if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)))
           break;
         tc_fence_after();
 #pragma unroll
-        for (int c0 = 0; c0 < HD; c0 += 32) {
+        for (int c0 = 0; c0 < OH; c0 += 32) {
           float v[32];
           tmem_ld32(to + c0, v);
 #pragma unroll
@@ -884,54 +982,62 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       const float mu = ref == -INFINITY ? 0.f : ref;
       // P buffer st is free once PV_{j-2} has completed
       if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[st], ((j >> 1) - 1) & 1))) break;
-      uint8_t* pb = smem + L::OFF_P + st * L::P_BYTES;
+      uint8_t* half = smem + L::OFF_P + st * L::P_BYTES + hh * L::HALF;
       float sum = 0.f;
 #pragma unroll
-      for (int c0 = 0; c0 < PT_KEYS; c0 += 32) {
-        uint32_t w[16];
+      for (int c8 = 0; c8 < 8; ++c8) {   // 8 keys = one 16-byte piece
+        uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2_approx(fmaf(s[c0 + e], sc, -mu));
-          const float p1 = ex2_approx(fmaf(s[c0 + e + 1], sc, -mu));
+        for (int e = 0; e < 8; e += 2) {
+          const float p0 = ex2_approx(fmaf(s[8 * c8 + e], sc, -mu));
+          const float p1 = ex2_approx(fmaf(s[8 * c8 + e + 1], sc, -mu));
           sum += p0 + p1;
           w[e >> 1] = pack_bf16x2(p0, p1);
         }
-        // 32 keys = 4 pieces of 16 bytes in the half of key c0 / 64
-        uint8_t* half = pb + (c0 >> 6) * L::HALF;
-        const int c8 = (c0 & 63) >> 3;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          *reinterpret_cast<uint4*>(half + sw128_off(r, c8 + k)) =
-              make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        *reinterpret_cast<uint4*>(half + sw128_off(r, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l += sum;
       tc_fence_before();               // the rescale's TMEM stores precede PV_j
       fence_proxy_async_smem();
       mbar_arrive(&p_full[st]);        // P_j is in shared memory
+      if (tracer) pt_tile(a, j, 6);
       done = j + 1;
     }
     if (done == n_tiles &&
         __all_sync(0xffffffffu, mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1))) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst =
-          a.out + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_out + (size_t)(kvh * G + R % G) * HD;
+      if (tracer) pt_clk(a, PT_TR_OREAD);
+      // every MMA is complete, so the Q tile is free: exchange the halves' sums
+      float* lpart = reinterpret_cast<float*>(smem + L::OFF_Q);
+      lpart[hh * PT_ROWS + r] = l;
+      mbar_arrive(l_ready);
+      const bool have = __all_sync(0xffffffffu, mbar_wait(l_ready, 0));
+      const float lt = lpart[r] + lpart[PT_ROWS + r];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      __nv_bfloat16* dst = a.out + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_out +
+                           (size_t)(kvh * G + R % G) * HD + hh * OH;
+      if (have) {
 #pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 32) {
-        float v[32];
-        tmem_ld32(to + c0, v);   // warp-collective: every lane loads
-        if (valid) {
+        for (int c0 = 0; c0 < OH; c0 += 32) {
+          float v[32];
+          tmem_ld32(to + c0, v);   // warp-collective: every lane loads
+          if (valid) {
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            uint4 u;
-            u.x = pack_bf16x2(v[c] * inv, v[c + 1] * inv);
-            u.y = pack_bf16x2(v[c + 2] * inv, v[c + 3] * inv);
-            u.z = pack_bf16x2(v[c + 4] * inv, v[c + 5] * inv);
-            u.w = pack_bf16x2(v[c + 6] * inv, v[c + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + c0 + c) = u;
+            for (int c = 0; c < 32; c += 8) {
+              uint4 u;
+              u.x = pack_bf16x2(v[c] * inv, v[c + 1] * inv);
+              u.y = pack_bf16x2(v[c + 2] * inv, v[c + 3] * inv);
+              u.z = pack_bf16x2(v[c + 4] * inv, v[c + 5] * inv);
+              u.w = pack_bf16x2(v[c + 6] * inv, v[c + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c0 + c) = u;
+            }
           }
         }
       }
+    }
+    if (tracer && a.trace != nullptr) {
+      pt_clk(a, PT_TR_CLK1);
+      pt_put(a, PT_TR_END, globaltimer_ns());
     }
   }
   if (warp == 1) pdl_wait();   // every CTA waits before it exits (PDL chain)
@@ -988,13 +1094,12 @@ static int prefill_tc_launch(const AttnArgs& a, int n_work, cudaStream_t st) {
   if (int rc = smem_attr_once(attn_prefill_tc_kernel<HD>, L::SMEM, attr_devs,
                               "prefill smem attribute"))
     return rc;
-  CUtensorMap map;
   const uint64_t rows = (uint64_t)a.num_blocks * 2 * a.n_kv_heads * a.block_size;
   if (rows >= (1ull << 31)) return arg_err("KV pool rows beyond 2^31");
-  int rc = make_tmap_2d(&map, a.pool, HD, rows, (uint64_t)HD * 2, 64, 16);
-  if (rc) return rc;
+  AttnArgs at = a;
+  at.trace = g_debug_trace;
   return launch_pdl(attn_prefill_tc_kernel<HD>, dim3(n_work, a.n_kv_heads), dim3(PT_THREADS),
-                    L::SMEM, st, 1, "attention prefill launch", map, a);
+                    L::SMEM, st, 1, "attention prefill launch", at);
 }
 
 static int check_common(const AttnArgs& a, int head_dim) {

@@ -29,6 +29,9 @@ struct AttnArgs {
   int* ws_count;            // [n_seqs, n_kv] split arrivals; zero between calls
   // prefill work list: pairs (seq, row tile)
   const int* work;
+  // debug timeline (tb_debug_trace) of the tcgen05 prefill: per CTA 16
+  // globaltimer stamps (PT_TR_*), or null
+  unsigned long long* trace;
 };
 
 int attn_decode(AttnArgs a, int head_dim, cudaStream_t st);

@@ -141,6 +141,8 @@ def paged_attention_decode(q, out, kv_pool, *, n_q_heads, n_kv_heads, head_dim, 
 
 def paged_attention_prefill(q, out, kv_pool, *, n_q_heads, n_kv_heads, head_dim, block_size,
                             block_tables, q_start, q_len, ctx_len, work):
+    if work.dim() != 2 or work.shape[1] != 2 or work.dtype != torch.int32:
+        raise ValueError("work must be an int32 [n_work, 2] tensor of (sequence, row tile)")
     lib = N.load()
     n = ctx_len.shape[0]
     N.check(lib.tb_paged_attention_prefill(
