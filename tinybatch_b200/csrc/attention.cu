@@ -27,8 +27,8 @@
 //   prefill         128 query rows per CTA (a work item (sequence, 128-row
 //                   tile) per kv head): for head_dim 64 / 128 and block sizes
 //                   that are multiples of 16 on tcgen05 (attn_prefill_tc_kernel:
-//                   TMA, S and O in TMEM); otherwise 8 warps of 16 rows on
-//                   mma.sync with key chunks shared by the warps.
+//                   cp.async gathers, S and O in TMEM); otherwise 8 warps of
+//                   16 rows on mma.sync with key chunks shared by the warps.
 #include "attention.cuh"
 #include "common.cuh"
 #include "host.h"
