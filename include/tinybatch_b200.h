@@ -261,9 +261,12 @@ int tb_argmax_vocab_parallel(void* comm, const float* logits, int ld, int M, int
  *   permutation): sequences are dispatched in this order (longest first
  *   keeps the tail of the launch short); NULL = index order.
  * _prefill: any q_len; work_pairs [n_work, 2] int32 = (seq, tile) with
- *   tiles of 128 query rows (row = token * Hq/Hkv + head in the group), best
- *   ordered longest first.  head_dim 64 / 128 with block_size a multiple of
- *   16 run on the tensor cores through TMA (tcgen05, S and O in TMEM). */
+ *   tiles of 256 query rows (row = token * Hq/Hkv + head in the group), best
+ *   ordered longest first; entries naming no sequence of the call, a tile
+ *   past its prompt, or a context longer than bt_ld blocks set
+ *   TB_STATUS_BAD_INDEX.  head_dim 64 / 128 with block_size a multiple of 16
+ *   run on the tensor cores (tcgen05: two 128-row tiles per CTA share each
+ *   K/V tile; S, P and O in TMEM). */
 size_t tb_attention_scratch_bytes(int n_seqs, int n_kv_heads, int head_dim, int max_ctx,
                                   int split_tokens);
 int tb_paged_attention_decode(const void* q, int ld_q, void* out, int ld_out,

@@ -114,11 +114,11 @@ def _loop_pack(token_ids, positions, slices, tables, ctx, bs, group, bt_width):
     d = subset(is_dec)
     p = subset(~is_dec)
     order = np.argsort(-d[2], kind="stable").astype(np.int32)
-    # (prefill sequence, 128-row tile), most keys read first (stable)
+    # (prefill sequence, 256-row tile), most keys read first (stable)
     tiles = []
     for r, (ql, c) in enumerate(zip(p[1].tolist(), p[2].tolist())):
-        for t in range(-(-ql * group // 128)):
-            last = min(t * 128 + 127, ql * group - 1)
+        for t in range(-(-ql * group // 256)):
+            last = min(t * 256 + 255, ql * group - 1)
             tiles.append((-min(c, c - ql + last // group + 1), len(tiles), r, t))
     work = np.asarray([(r, t) for *_, r, t in sorted(tiles)], dtype=np.int32).reshape(-1, 2)
     return np.concatenate([ids, pos, slots, row_dst, d[0], d[1], d[2], d[3].ravel(), order,
@@ -170,7 +170,7 @@ def test_token_view_matches_list():
 
 
 def test_prefill_work_list():
-    """(sequence, 128-row tile) pairs covering every query row once, ordered
+    """(sequence, 256-row tile) pairs covering every query row once, ordered
     by the keys a tile reads (its last row's causal limit), most first."""
     from tinybatch_b200.runtime import PREFILL_ROWS, prefill_work
     q_len, ctx, G = [300, 5, 64, 1], [300, 900, 64, 40], 5

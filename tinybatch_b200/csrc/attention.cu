@@ -24,7 +24,7 @@
 //                   TMA (a producer warp, 8-slot mbarrier ring) when the
 //                   block size is a multiple of 16 and hd is 64 or 128,
 //                   else by per-lane cp.async.
-//   prefill         128 query rows per CTA (a work item (sequence, 128-row
+//   prefill         256 query rows per CTA (a work item (sequence, 256-row
 //                   tile) per kv head): for head_dim 64 / 128 and block sizes
 //                   that are multiples of 16 on tcgen05 (attn_prefill_tc_kernel:
 //                   cp.async gathers, S and O in TMEM); otherwise 8 warps of
@@ -534,14 +534,16 @@ __global__ void __launch_bounds__(TMA_THREADS, 3)
 
 constexpr int PF_STAGES = 2;
 
-// A prefill work item (sequence, 128-row tile) that names a sequence of the
+constexpr int PF_ROWS = 256;   // query rows per prefill work item
+
+// A prefill work item (sequence, 256-row tile) that names a sequence of the
 // call, a row tile inside its prompt, a prompt no longer than its context and
 // a context its block-table row can hold.
 __device__ __forceinline__ bool prefill_item_ok(const AttnArgs& a, int seq, int rt) {
   if (seq < 0 || seq >= a.n_seqs || rt < 0) return false;
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
-  return qlen >= 1 && qlen <= ctx && rt * 128 < qlen * G &&
+  return qlen >= 1 && qlen <= ctx && rt * PF_ROWS < qlen * G &&
          (ctx + a.block_size - 1) / a.block_size <= a.bt_ld;
 }
 
@@ -561,12 +563,16 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
   const int ctx = a.ctx_len[seq], qlen = a.q_len[seq], q0 = a.q_start[seq];
   const int G = a.n_q_heads / a.n_kv_heads;
   const int nrows_total = qlen * G;
-  const int row0 = rt * 128 + warp * 16;
+  // the work item's rows in two passes of 128 (8 warps x 16 rows)
+  for (int sub = 0; sub < PF_ROWS / 128; ++sub) {
+  const int r128 = rt * (PF_ROWS / 128) + sub;
+  if (r128 * 128 >= nrows_total) break;
+  const int row0 = r128 * 128 + warp * 16;
   const int nrows = max(0, min(16, nrows_total - row0));
   const int first = ctx - qlen;
   const int* table = a.block_tables + (size_t)seq * a.bt_ld;
   // keys needed by the whole CTA: up to the last row's causal limit
-  const int last_row = min(rt * 128 + 127, nrows_total - 1);
+  const int last_row = min(r128 * 128 + 127, nrows_total - 1);
   const int cta_keys = min(ctx, first + last_row / G + 1);
   const int n_chunks = (cta_keys + 15) / 16;
 
@@ -614,51 +620,52 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
           pack_bf16x2(f.o[nt][2 * h] * inv, f.o[nt][2 * h + 1] * inv);
     }
   }
+  __syncthreads();   // the next pass refills the chunk ring
+  }
 }
 
 // ------------------------------------------------------ prefill, tcgen05
 //
-// One CTA per (work item = (sequence, 128-row tile), kv head).  Row r of the
-// tile is query row R = 128 * tile + r: token R / G, head R % G of the kv
-// head's group.  Keys go in tiles of 128 (8 chunks of 16 tokens, each chunk
-// one block-table lookup), up to the last row's causal limit.
+// One CTA per (work item = (sequence, 256-row tile), kv head): two query
+// tiles A and B of 128 rows share every K/V tile.  Row r of tile x is query
+// row R = 256 * tile + 128 * x + r: token R / G, head R % G of the kv head's
+// group.  Keys go in tiles of 128 (8 chunks of 16 tokens, each chunk one
+// block-table lookup), up to the last row's causal limit.
 //   warps 0/10 loaders of K / V: every key tile gathered from the pool
 //              through the block table with 16-byte cp.async pieces (a warp
 //              instruction moves two whole 256-byte key rows), written in the
 //              128-byte-swizzled layout the MMA descriptors describe, into
-//              two-stage rings (a K stage is refilled as soon as its S MMA is
-//              done, a V stage once its PV MMA is done).  A tile's barrier
-//              completes when its pieces have landed (cp.async arrivals), and
-//              the MMA thread fences them over to the async proxy.  (TMA boxes of one 16-token block half -- 2 KiB,
-//              all the pool keeps contiguous at block size 16 -- issued at
-//              ~40 ns each from one thread, left the tensor pipe waiting.)
-//   warp 1     TMEM owner and MMA issuer: S_j = Q K_j^T (M 128, N 128 keys,
-//              K = HD) into one of two TMEM S buffers, two tiles ahead of the
-//              softmax; once P_j is in shared memory, O += P_j V_j (M 128,
-//              N = HD, K 128 keys) into the TMEM O accumulator, V read in
-//              place as an MN-major operand
-//   warps 2-9  two threads per query row (TMEM lane = row; warps w and w + 4
-//              share a lane quarter): Q into shared memory, then per key tile
-//              the row max over all 128 scores (each thread reads both
-//              halves), and for its own half of the keys P_j = exp2(S_j -
-//              ref) as bf16 into one of two shared-memory P buffers and its
-//              part of the running sum
-// O stays in TMEM across the key tiles.  A row's exponent reference `ref`
+//              two-stage rings (a K stage is refilled once both S MMAs of
+//              its tile are done, a V stage once both PV MMAs are done).  A
+//              stage's barrier completes when its pieces have landed
+//              (cp.async arrivals) and the MMA thread fences them over to
+//              the async proxy.  (TMA boxes of one 16-token block half --
+//              2 KiB, all the pool keeps contiguous at block size 16 --
+//              issued at ~40 ns each from one thread, left the tensor pipe
+//              waiting.)
+//   warp 1     TMEM owner and MMA issuer.  Per query tile x: S_x = Q_x K_j^T
+//              (M 128, N 128 keys, K = HD) into S_x in TMEM; once the
+//              softmax has written P_x (bf16, over the first 64 columns of
+//              S_x), O_x += P_x V_j with P read from TMEM and V in place as
+//              an MN-major operand; S_x for the next key tile follows once
+//              that PV is complete (it overwrites P_x).  The two tiles'
+//              chains interleave, so one tile's MMAs run while the other's
+//              softmax works.
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per
+//              thread (TMEM lane = row): Q into shared memory, then per key
+//              tile the row's 128 scores into registers, the row max, P =
+//              exp2(S - ref) into TMEM, and the running sum
+// O_x stays in TMEM across the key tiles.  A row's exponent reference `ref`
 // moves only when its running max exceeds it by more than PT_RESCALE (log2
 // units): then the row's O is rescaled in TMEM (after the PV MMAs issued so
-// far complete; each of its two threads scales half the columns) and its
-// sums by the same factor.  Otherwise P and O carry a factor of at most
-// 2^PT_RESCALE, which the final division by the sum removes; bf16 rounding
-// of P is relative, so the factor costs no precision.  Both threads of a row
-// see the same scores and take the same decisions.
+// far complete) and its sum by the same factor.  Otherwise P and O carry a
+// factor of at most 2^PT_RESCALE, which the final division by the sum
+// removes; bf16 rounding of P is relative, so the factor costs no precision.
 // Shared-memory tiles use the 128-byte swizzle (rows of 64 bf16, 16-byte
-// pieces XOR-permuted by row % 8, 8-row atoms 1024 B apart), the layout TMA
-// writes and the MMA descriptors describe; Q and P are written by threads in
-// the same layout.
-constexpr int PT_ROWS = 128;     // query rows per CTA
+// pieces XOR-permuted by row % 8, 8-row atoms 1024 B apart).
+constexpr int PT_ROWS = 128;     // query rows per tile (two tiles per CTA)
 constexpr int PT_KEYS = 128;     // keys per tile
-constexpr int PT_THREADS = 352;  // K loader, MMA, 8 softmax warps, V loader
-constexpr int PT_SOFT = 256;     // softmax threads
+constexpr int PT_THREADS = 352;  // K loader, MMA, 2 x 4 softmax warps, V loader
 constexpr float PT_RESCALE = 8.f;
 
 // Debug timeline of a prefill CTA (tb_debug_trace), PT_TR_POINTS slots:
@@ -667,8 +674,8 @@ constexpr float PT_RESCALE = 8.f;
 // cycles): 1 Q stored, 26 the MMA thread sees Q, 27 the output is read from
 // TMEM, and for key tiles k < 3 at 2 + 8k: +0 / +1 K_k loads start / issued,
 // +2 / +3 V_k loads start / issued (loaders; start = its stage is free),
-// +4 S_k issued (MMA), +5 S_k in registers, +6 P_k stored (softmax), +7 PV_k
-// issued (MMA).
+// +4 S_A,k issued (MMA), +5 S_A,k in registers, +6 P_A,k stored (first
+// softmax thread), +7 PV_A,k issued (MMA).
 enum : int { PT_TR_Q = 1, PT_TR_TILES = 3, PT_TR_QSEEN = 26, PT_TR_OREAD = 27, PT_TR_CLK1 = 29,
              PT_TR_CLK0 = 30, PT_TR_END = 31, PT_TR_POINTS = 32 };
 
@@ -687,22 +694,21 @@ template <int HD>
 struct PrefillTcLayout {
   static constexpr int HALVES = HD / 64;                  // 64-column halves
   static constexpr int HALF = PT_ROWS * 128;              // one [128][64] bf16 half: 16 KiB
-  static constexpr int Q_BYTES = HALVES * HALF;
+  static constexpr int Q_TILE = HALVES * HALF;
   static constexpr int KV_HALF = PT_KEYS * 128;           // [128 keys][64] bf16
   static constexpr int KV_PART = HALVES * KV_HALF;        // K (or V) of one key tile
   static constexpr int STAGE = 2 * KV_PART;               // K then V
-  static constexpr int P_BYTES = 2 * HALF;                // [128 rows][128 keys] bf16
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_KV = Q_BYTES;
-  static constexpr int OFF_P = OFF_KV + 2 * STAGE;        // two P buffers
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-  static constexpr int N_BARS = 19;
+  static constexpr int OFF_Q = 0;                         // Q_A then Q_B
+  static constexpr int OFF_KV = 2 * Q_TILE;
+  static constexpr int OFF_BAR = OFF_KV + 2 * STAGE;
+  static constexpr int N_BARS = 17;
   static constexpr int SMEM = OFF_BAR + 24 * 8 + 1024;     // barriers + TMEM slot + alignment slack
-  static constexpr uint32_t TMEM_COLS = 512;              // S0, S1, O
-  static constexpr uint32_t COL_S0 = 0, COL_S1 = PT_KEYS, COL_O = 2 * PT_KEYS;
-  static_assert(COL_O + HD <= TMEM_COLS, "TMEM: two S buffers and O");
+  static constexpr uint32_t TMEM_COLS = 512;
+  // S_A, S_B (P_x over the first 64 columns of S_x), O_A, O_B
+  __device__ static constexpr uint32_t col_s(int x) { return (uint32_t)(x * PT_KEYS); }
+  __device__ static constexpr uint32_t col_o(int x) { return (uint32_t)(2 * PT_KEYS + x * HD); }
+  static_assert(2 * PT_KEYS + 2 * HD <= TMEM_COLS, "TMEM: two S and two O");
   static_assert(N_BARS * 8 + 4 <= 24 * 8, "barrier area");
-  static_assert(2 * PT_ROWS * 4 <= Q_BYTES, "the final sum exchange reuses the Q tile");
   static_assert(SMEM <= 232448, "prefill shared memory above 227 KiB");
 };
 
@@ -718,17 +724,15 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* k_full = bars;         // [2]
+  uint64_t* k_full = bars;         // [2] by stage
   uint64_t* k_empty = bars + 2;    // [2]
   uint64_t* v_full = bars + 4;     // [2]
   uint64_t* v_empty = bars + 6;    // [2]
-  uint64_t* s_full = bars + 8;     // [2]
-  uint64_t* s_free = bars + 10;    // [2]
-  uint64_t* p_full = bars + 12;    // [2]
-  uint64_t* pv_done = bars + 14;   // [2]
-  uint64_t* q_full = bars + 16;
-  uint64_t* mma_idle = bars + 17;  // every MMA of the CTA complete (before TMEM is freed)
-  uint64_t* l_ready = bars + 18;   // both partial sums of every row stored
+  uint64_t* s_full = bars + 8;     // [2] by query tile
+  uint64_t* p_full = bars + 10;    // [2] by query tile: P written, S read
+  uint64_t* pv_done = bars + 12;   // [2] by query tile
+  uint64_t* q_full = bars + 14;
+  uint64_t* mma_idle = bars + 15;  // every MMA of the CTA complete (before TMEM is freed)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -745,9 +749,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   const int G = a.n_q_heads / a.n_kv_heads;
   const int nrows_total = qlen * G;
   const int first = ctx - qlen;
-  const int last_row = min(rt * PT_ROWS + PT_ROWS - 1, nrows_total - 1);
+  const int last_row = min(rt * PF_ROWS + PF_ROWS - 1, nrows_total - 1);
   const int keys = max(1, min(ctx, first + last_row / G + 1));   // keys this CTA needs
   const int n_tiles = (keys + PT_KEYS - 1) / PT_KEYS;
+  const bool has_b = rt * PF_ROWS + PT_ROWS < nrows_total;      // tile B holds a row
   const int* table = a.block_tables + (size_t)seq * a.bt_ld;
 
   if (threadIdx.x == 0) {
@@ -757,13 +762,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       mbar_init(&v_full[i], 32);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], PT_SOFT);
-      mbar_init(&p_full[i], PT_SOFT);
+      mbar_init(&p_full[i], PT_ROWS);
       mbar_init(&pv_done[i], 1);
     }
-    mbar_init(q_full, PT_SOFT);
+    mbar_init(q_full, 2 * PT_ROWS);
     mbar_init(mma_idle, 1);
-    mbar_init(l_ready, PT_SOFT);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -833,65 +836,77 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_m128(PT_KEYS);
       constexpr uint32_t idesc_o = idesc_bf16_m128(HD) | (1u << 16);   // B (V) MN-major
-      const uint32_t qbase = sbase + L::OFF_Q;
       bool ok = mbar_wait(q_full, 0);
       tc_fence_after();
       pt_clk(a, PT_TR_QSEEN);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
-        if (j >= 2 && !mbar_wait(&s_free[st], ((j >> 1) - 1) & 1)) return false;
-        tc_fence_after();
-        fence_proxy_async_smem();   // K arrived through cp.async (generic proxy)
-        const uint32_t kbase = sbase + L::OFF_KV + st * L::STAGE;
+      const int nx = has_b ? 2 : 1;
+      auto issue_s = [&](int x, int j) {
+        const uint32_t qbase = sbase + L::OFF_Q + x * L::Q_TILE;
+        const uint32_t kbase = sbase + L::OFF_KV + (j & 1) * L::STAGE;
 #pragma unroll
         for (int h = 0; h < L::HALVES; ++h)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc_mma_bf16(tmem + (st ? L::COL_S1 : L::COL_S0),
-                        sw128_desc(qbase + h * L::HALF + kk * 32),
+            tc_mma_bf16(tmem + L::col_s(x), sw128_desc(qbase + h * L::HALF + kk * 32),
                         sw128_desc(kbase + h * L::KV_HALF + kk * 32), idesc_s,
                         (h | kk) ? 1u : 0u);
-        tc_commit(&k_empty[st]);
-        tc_commit(&s_full[st]);
-        pt_tile(a, j, 4);
-        return true;
+        tc_commit(&s_full[x]);
+        if (x == 0) pt_tile(a, j, 4);
       };
-      auto issue_pv = [&](int t) -> bool {
-        const int b = t & 1;
-        if (!mbar_wait(&v_full[b], (t >> 1) & 1) || !mbar_wait(&p_full[b], (t >> 1) & 1))
-          return false;
+      auto issue_pv = [&](int x, int j) -> bool {
+        if (!mbar_wait(&p_full[x], j & 1)) return false;
         tc_fence_after();
-        fence_proxy_async_smem();   // V arrived through cp.async (generic proxy)
-        const uint32_t vbase = sbase + L::OFF_KV + b * L::STAGE + L::KV_PART;
-        const uint32_t pbase = sbase + L::OFF_P + b * L::P_BYTES;
+        const uint32_t vbase = sbase + L::OFF_KV + (j & 1) * L::STAGE + L::KV_PART;
 #pragma unroll
-        for (int ks = 0; ks < PT_KEYS / 16; ++ks) {
-          const uint64_t ad = sw128_desc(pbase + (ks >> 2) * L::HALF + (ks & 3) * 32);
-          const uint64_t bd = sw128_mn_desc(vbase + ks * 2048, L::KV_HALF, 1024);
-          tc_mma_bf16(tmem + L::COL_O, ad, bd, idesc_o, (t > 0 || ks > 0) ? 1u : 0u);
-        }
-        tc_commit(&v_empty[b]);
-        tc_commit(&pv_done[b]);
-        pt_tile(a, t, 7);
+        for (int ks = 0; ks < PT_KEYS / 16; ++ks)
+          tc_mma_bf16_ts(tmem + L::col_o(x), tmem + L::col_s(x) + ks * 8,
+                         sw128_mn_desc(vbase + ks * 2048, L::KV_HALF, 1024), idesc_o,
+                         (j > 0 || ks > 0) ? 1u : 0u);
+        tc_commit(&pv_done[x]);
+        if (x == 0) pt_tile(a, j, 7);
         return true;
       };
-      // S runs two tiles ahead of the softmax; PV_t goes out as soon as P_t is in
-      for (int j = 0; j < 2 && j < n_tiles && ok; ++j) ok = issue_s(j);
-      for (int t = 0; t < n_tiles && ok; ++t) {
-        ok = issue_pv(t);
-        if (ok && t + 2 < n_tiles) ok = issue_s(t + 2);
+      if (ok) ok = mbar_wait(&k_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        fence_proxy_async_smem();   // K arrived through cp.async (generic proxy)
+        for (int x = 0; x < nx; ++x) issue_s(x, 0);
+        tc_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const bool next = j + 1 < n_tiles;
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1)) break;
+        fence_proxy_async_smem();   // V arrived through cp.async (generic proxy)
+        bool k_ready = false;
+        for (int x = 0; x < nx && ok; ++x) {
+          ok = issue_pv(x, j);
+          if (!ok || !next) continue;
+          if (!k_ready) {
+            ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1);
+            fence_proxy_async_smem();
+            k_ready = true;
+          }
+          // S_x of the next key tile overwrites P_x: issue it once PV_x is done
+          if (ok) ok = mbar_wait(&pv_done[x], j & 1);
+          if (ok) {
+            tc_fence_after();
+            issue_s(x, j + 1);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&v_empty[j & 1]);
+        if (next) tc_commit(&k_empty[(j + 1) & 1]);
       }
       tc_commit(mma_idle);
       mbar_wait(mma_idle, 0);
     }
   } else {
-    // ---------------- softmax: two threads per query row
+    // ---------------- softmax: one query row per thread, tile x
+    const int x = (warp - 2) >> 2;
     const int q4 = warp & 3;
-    const int hh = (warp - 2) >> 2;               // which half of the keys (and of O)
     const int r = q4 * 32 + lane;                 // TMEM lane of this thread
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const int R = rt * PT_ROWS + r;
+    const int R = rt * PF_ROWS + x * PT_ROWS + r;
     const bool valid = R < nrows_total;
     const int limit = valid ? first + R / G : -1;   // last key this row sees
     const bool tracer = threadIdx.x == 64;
@@ -901,124 +916,97 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     }
     pdl_wait();   // q is written by the previous kernel
     {
-      uint8_t* qs = smem + L::OFF_Q;
+      uint8_t* qs = smem + L::OFF_Q + x * L::Q_TILE;
       const __nv_bfloat16* src =
           a.q + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_q + (size_t)(kvh * G + R % G) * HD;
-      uint4 v[HD / 16];
+      uint4 v[HD / 8];
 #pragma unroll
-      for (int i = 0; i < HD / 16; ++i) {
-        const int c = hh * (HD / 16) + i;
-        v[i] = valid ? *reinterpret_cast<const uint4*>(src + c * 8) : make_uint4(0u, 0u, 0u, 0u);
-      }
+      for (int c = 0; c < HD / 8; ++c)
+        v[c] = valid ? *reinterpret_cast<const uint4*>(src + c * 8) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int i = 0; i < HD / 16; ++i) {
-        const int c = hh * (HD / 16) + i;
-        *reinterpret_cast<uint4*>(qs + (c >> 3) * L::HALF + sw128_off(r, c & 7)) = v[i];
-      }
+      for (int c = 0; c < HD / 8; ++c)
+        *reinterpret_cast<uint4*>(qs + (c >> 3) * L::HALF + sw128_off(r, c & 7)) = v[c];
       fence_proxy_async_smem();
       mbar_arrive(q_full);
       if (tracer) pt_clk(a, PT_TR_Q);
     }
-    constexpr int OH = HD / 2;                    // O columns of this thread
-    const uint32_t to = tmem + L::COL_O + (uint32_t)(hh * OH) + lane_off;
-    float ref = -INFINITY, l = 0.f;   // exponent reference (log2 units) and this half's sum
-    const float sc = a.scale_log2;
-    int done = 0;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      // waits are made warp-uniform: the TMEM accesses below are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1))) break;
-      tc_fence_after();
-      const int k0 = j * PT_KEYS;
-      const uint32_t ts = tmem + (st ? L::COL_S1 : L::COL_S0) + lane_off;
-      float s[64];
-      float mx = -INFINITY;
-      tmem_ld64(ts + hh * 64, s);
-      {
-        // the other half's scores, for the row max only
-        const int ko = k0 + (1 - hh) * 64;
-#pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 32) {
-          float o[32];
-          tmem_ld32(ts + (1 - hh) * 64 + c0, o);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, ko + c0 + e <= limit ? o[e] : -INFINITY);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&s_free[st]);        // S buffer st may be overwritten
-      if (tracer) pt_tile(a, j, 5);
-      const int ks = k0 + hh * 64;
-      if (ks + 63 > limit) {           // the causal edge (or an empty row)
-#pragma unroll
-        for (int e = 0; e < 64; ++e)
-          if (ks + e > limit) s[e] = -INFINITY;
-      }
-#pragma unroll
-      for (int e = 0; e < 64; ++e) mx = fmaxf(mx, s[e]);
-      mx *= sc;
-      const bool move = mx > ref + PT_RESCALE;   // any finite max when ref is -inf
-      const bool rescale = move && ref != -INFINITY;
-      const float alpha = rescale ? ex2_approx(ref - mx) : 1.f;
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O holds PV_0 .. PV_{j-1}: once the last of them is complete, scale
-        // this thread's half of its row in place (alpha = 1 for rows that
-        // keep their ref)
-        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)))
-          break;
+    if (x == 1 && !has_b) {
+      // no row of tile B: nothing to compute
+    } else {
+      const uint32_t ts = tmem + L::col_s(x) + lane_off;   // S_x, and P_x over its first 64 columns
+      const uint32_t to = tmem + L::col_o(x) + lane_off;
+      float ref = -INFINITY, l = 0.f;   // exponent reference (log2 units) and running sum
+      const float sc = a.scale_log2;
+      int done = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        // waits are made warp-uniform: the TMEM accesses below are warp-collective
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1))) break;
         tc_fence_after();
+        float s[PT_KEYS];
+        tmem_ld64(ts, s);
+        tmem_ld64(ts + 64, s + 64);
+        if (tracer) pt_tile(a, j, 5);
+        const int k0 = j * PT_KEYS;
+        if (k0 + PT_KEYS - 1 > limit) {   // the causal edge (or an empty row)
 #pragma unroll
-        for (int c0 = 0; c0 < OH; c0 += 32) {
-          float v[32];
-          tmem_ld32(to + c0, v);
+          for (int e = 0; e < PT_KEYS; ++e)
+            if (k0 + e > limit) s[e] = -INFINITY;
+        }
+        float mx = -INFINITY;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] *= alpha;
-          tmem_st32(to + c0, v);
+        for (int e = 0; e < PT_KEYS; e += 2) mx = fmax3(mx, s[e], s[e + 1]);
+        mx *= sc;
+        const bool move = mx > ref + PT_RESCALE;   // any finite max when ref is -inf
+        const bool rescale = move && ref != -INFINITY;
+        const float alpha = rescale ? ex2_approx(ref - mx) : 1.f;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O holds PV_0 .. PV_{j-1}: once the last of them is complete,
+          // scale the warp's rows in place (alpha = 1 for rows that keep
+          // their ref)
+          if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[x], (j - 1) & 1))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c0 = 0; c0 < HD; c0 += 32) {
+            float v[32];
+            tmem_ld32(to + c0, v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= alpha;
+            tmem_st32(to + c0, v);
+          }
+        }
+        if (move) ref = mx;
+        l *= alpha;
+        const float mu = ref == -INFINITY ? 0.f : ref;
+        const float2 sc2 = make_float2(sc, sc), nmu2 = make_float2(-mu, -mu);
+        float2 sum2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c0 = 0; c0 < PT_KEYS; c0 += 32) {
+          uint32_t w[16];   // 32 keys, two bf16 per 32-bit column
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 xv = fma2(make_float2(s[c0 + e], s[c0 + e + 1]), sc2, nmu2);
+            const float2 pv = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
+            sum2 = add2(sum2, pv);
+            w[e >> 1] = pack_bf16x2(pv.x, pv.y);
+          }
+          tmem_st16(ts + (c0 >> 1), w);
         }
         tmem_wait_st();
+        l += sum2.x + sum2.y;
+        tc_fence_before();               // P (and a rescaled O) precede PV
+        mbar_arrive(&p_full[x]);         // P_x is in TMEM, S_x has been read
+        if (tracer) pt_tile(a, j, 6);
+        done = j + 1;
       }
-      if (move) ref = mx;
-      l *= alpha;
-      const float mu = ref == -INFINITY ? 0.f : ref;
-      // P buffer st is free once PV_{j-2} has completed
-      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[st], ((j >> 1) - 1) & 1))) break;
-      uint8_t* half = smem + L::OFF_P + st * L::P_BYTES + hh * L::HALF;
-      float sum = 0.f;
+      if (done == n_tiles &&
+          __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (n_tiles - 1) & 1))) {
+        tc_fence_after();
+        if (tracer) pt_clk(a, PT_TR_OREAD);
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* dst = a.out + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_out +
+                             (size_t)(kvh * G + R % G) * HD;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {   // 8 keys = one 16-byte piece
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const float p0 = ex2_approx(fmaf(s[8 * c8 + e], sc, -mu));
-          const float p1 = ex2_approx(fmaf(s[8 * c8 + e + 1], sc, -mu));
-          sum += p0 + p1;
-          w[e >> 1] = pack_bf16x2(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(half + sw128_off(r, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      l += sum;
-      tc_fence_before();               // the rescale's TMEM stores precede PV_j
-      fence_proxy_async_smem();
-      mbar_arrive(&p_full[st]);        // P_j is in shared memory
-      if (tracer) pt_tile(a, j, 6);
-      done = j + 1;
-    }
-    if (done == n_tiles &&
-        __all_sync(0xffffffffu, mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1))) {
-      tc_fence_after();
-      if (tracer) pt_clk(a, PT_TR_OREAD);
-      // every MMA is complete, so the Q tile is free: exchange the halves' sums
-      float* lpart = reinterpret_cast<float*>(smem + L::OFF_Q);
-      lpart[hh * PT_ROWS + r] = l;
-      mbar_arrive(l_ready);
-      const bool have = __all_sync(0xffffffffu, mbar_wait(l_ready, 0));
-      const float lt = lpart[r] + lpart[PT_ROWS + r];
-      const float inv = lt > 0.f ? 1.f / lt : 0.f;
-      __nv_bfloat16* dst = a.out + (size_t)(q0 + (valid ? R / G : 0)) * a.ld_out +
-                           (size_t)(kvh * G + R % G) * HD + hh * OH;
-      if (have) {
-#pragma unroll
-        for (int c0 = 0; c0 < OH; c0 += 32) {
+        for (int c0 = 0; c0 < HD; c0 += 32) {
           float v[32];
           tmem_ld32(to + c0, v);   // warp-collective: every lane loads
           if (valid) {

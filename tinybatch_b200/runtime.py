@@ -238,11 +238,11 @@ def rope_tables(cfg: ModelConfig, device) -> tuple[torch.Tensor, torch.Tensor]:
 
 # ------------------------------------------------------------------ metadata
 
-PREFILL_ROWS = 128      # query rows per prefill attention work item
+PREFILL_ROWS = 256      # query rows per prefill attention work item (two 128-row tiles)
 
 
 def prefill_work(q_len, ctx, group: int) -> np.ndarray:
-    """Prefill attention work list: (sequence, tile of 128 query rows) pairs,
+    """Prefill attention work list: (sequence, tile of 256 query rows) pairs,
     row = token * group + head, ordered by the keys each tile reads (its last
     row's causal limit), most first, so long tiles start early."""
     items, cost = [], []
@@ -266,7 +266,7 @@ class StepMeta:
     sequence's last token, else -1); for the decode subset (q_len*G <= 16)
     and the prefill subset: q_start, q_len, ctx_len [n], block tables
     [n, bt_ld] (-1 padded); the decode subset's order by descending context
-    length; the prefill (sequence, 128-row tile) work list (``prefill_work``)."""
+    length; the prefill (sequence, 256-row tile) work list (``prefill_work``)."""
 
     def __init__(self, token_ids, positions, seq_slices, block_tables, context_lens,
                  block_size: int, group: int, device, pinned: bool = True,
