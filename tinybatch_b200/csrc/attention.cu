@@ -631,7 +631,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
 // row R = 256 * tile + 128 * x + r: token R / G, head R % G of the kv head's
 // group.  Keys go in tiles of 128 (8 chunks of 16 tokens, each chunk one
 // block-table lookup), up to the last row's causal limit.
-//   warps 0/10 loaders of K / V: every key tile gathered from the pool
+//   warps 0/2  loaders of K / V: every key tile gathered from the pool
 //              through the block table with 16-byte cp.async pieces (a warp
 //              instruction moves two whole 256-byte key rows), written in the
 //              128-byte-swizzled layout the MMA descriptors describe, into
@@ -651,7 +651,9 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
 //              that PV is complete (it overwrites P_x).  The two tiles'
 //              chains interleave, so one tile's MMAs run while the other's
 //              softmax works.
-//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per
+//   warp 3     spare: completes the first warpgroup, whose registers go to
+//              the softmax warpgroups (setmaxnreg)
+//   warps 4-7  softmax of tile A, warps 8-11 of tile B: one query row per
 //              thread (TMEM lane = row): Q into shared memory, then per key
 //              tile the row's 128 scores into registers, the row max, P =
 //              exp2(S - ref) into TMEM, and the running sum
@@ -665,7 +667,14 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnArgs a) {
 // pieces XOR-permuted by row % 8, 8-row atoms 1024 B apart).
 constexpr int PT_ROWS = 128;     // query rows per tile (two tiles per CTA)
 constexpr int PT_KEYS = 128;     // keys per tile
-constexpr int PT_THREADS = 352;  // K loader, MMA, 2 x 4 softmax warps, V loader
+constexpr int PT_THREADS = 384;  // K loader, MMA, V loader, spare; 2 x 4 softmax warps
+// Registers per thread: the launch gives every thread PT_REGS_LAUNCH; the
+// first warpgroup (loaders, MMA) drops to PT_REGS_LOW and the two softmax
+// warpgroups rise to PT_REGS_HIGH, so a row's 128 scores stay in registers
+// without spilling.
+constexpr int PT_REGS_LAUNCH = 168, PT_REGS_LOW = 56, PT_REGS_HIGH = 224;
+static_assert(128 * PT_REGS_LOW + 256 * PT_REGS_HIGH <= PT_THREADS * PT_REGS_LAUNCH,
+              "register split above the launch total");
 constexpr float PT_RESCALE = 8.f;
 
 // Debug timeline of a prefill CTA (tb_debug_trace), PT_TR_POINTS slots:
@@ -780,8 +789,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
   if (threadIdx.x == 0) pdl_trigger();
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == 0 || warp == PT_THREADS / 32 - 1) {
-    // ---------------- loaders: K (warp 0) and V (the last warp)
+  if (warp < 4) {
+  setmaxnreg_dec<PT_REGS_LOW>();
+  if (warp == 0 || warp == 2) {
+    // ---------------- loaders: K (warp 0) and V (warp 2)
     const int is_v = warp != 0;
     uint64_t* full = is_v ? v_full : k_full;
     uint64_t* empty = is_v ? v_empty : k_empty;
@@ -900,16 +911,18 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
       tc_commit(mma_idle);
       mbar_wait(mma_idle, 0);
     }
+  }   // warp 3: nothing to do
   } else {
+    setmaxnreg_inc<PT_REGS_HIGH>();
     // ---------------- softmax: one query row per thread, tile x
-    const int x = (warp - 2) >> 2;
+    const int x = (warp - 4) >> 2;
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;                 // TMEM lane of this thread
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const int R = rt * PF_ROWS + x * PT_ROWS + r;
     const bool valid = R < nrows_total;
     const int limit = valid ? first + R / G : -1;   // last key this row sees
-    const bool tracer = threadIdx.x == 64;
+    const bool tracer = threadIdx.x == 128;
     if (tracer && a.trace != nullptr) {
       pt_put(a, 0, globaltimer_ns());
       pt_clk(a, PT_TR_CLK0);
@@ -1082,6 +1095,17 @@ static int prefill_tc_launch(const AttnArgs& a, int n_work, cudaStream_t st) {
   if (int rc = smem_attr_once(attn_prefill_tc_kernel<HD>, L::SMEM, attr_devs,
                               "prefill smem attribute"))
     return rc;
+  // the softmax warpgroups' setmaxnreg.inc waits for registers the first
+  // warpgroup releases: refuse a build whose launch total cannot cover it
+  static std::atomic<int> regs_ok{0};
+  if (!regs_ok.load(std::memory_order_acquire)) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, attn_prefill_tc_kernel<HD>);
+    if (e != cudaSuccess) return host_err(e, "prefill attributes");
+    if (fa.numRegs * PT_THREADS < 128 * PT_REGS_LOW + 256 * PT_REGS_HIGH)
+      return arg_err("prefill kernel built with too few registers for its register split");
+    regs_ok.store(1, std::memory_order_release);
+  }
   const uint64_t rows = (uint64_t)a.num_blocks * 2 * a.n_kv_heads * a.block_size;
   if (rows >= (1ull << 31)) return arg_err("KV pool rows beyond 2^31");
   AttnArgs at = a;

@@ -351,6 +351,20 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   return f2_unpack(d);
 }
 
+// Register reallocation between the warpgroups of a CTA (all 128 threads of
+// a warpgroup execute the same instruction).  inc waits until enough
+// registers have been released by dec in other warpgroups: the launch total
+// (threads x registers per thread at launch) must cover every warpgroup's
+// share, which the launcher checks before the first launch.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Make this thread's generic-proxy writes to shared memory visible to the
 // async proxy (tcgen05.mma operands written by threads, not by TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
