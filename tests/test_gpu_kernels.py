@@ -300,6 +300,27 @@ def test_paged_attention_prefill_long(hq, hkv, hd, bs):
         torch.testing.assert_close(out.float().cpu(), ref, atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("hq,hkv,hd,bs", [(40, 8, 128, 16), (4, 2, 16, 4)])
+def test_paged_attention_prefill_rejects_bad_work(hq, hkv, hd, bs):
+    """Work entries naming no sequence of the call, a row tile past the prompt
+    or a negative tile are refused in the kernel (status BAD_INDEX, nothing
+    read through them, valid entries of the same call still computed)."""
+    q_lens, ctx = [40, 7], [40, 30]
+    d, ref = _paged_case(hq, hkv, hd, bs, q_lens, ctx, seed=5)
+    G = hq // hkv
+    good = prefill_work(q_lens, ctx, G).tolist()
+    bad = [[2, 0], [0, 5], [1, -1]]
+    work = torch.tensor(good + bad, dtype=torch.int32, device=DEV)
+    out = torch.zeros(sum(q_lens), hq * hd, dtype=torch.bfloat16, device=DEV)
+    ops.paged_attention_prefill(d["q"], out, d["pool"], n_q_heads=hq, n_kv_heads=hkv,
+                                head_dim=hd, block_size=bs, block_tables=d["bt"],
+                                q_start=d["q_start"], q_len=d["q_len"], ctx_len=d["ctx"],
+                                work=work)
+    torch.cuda.synchronize()
+    assert _native.status(clear=True) == 103      # TB_STATUS_BAD_INDEX
+    torch.testing.assert_close(out.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
 def test_embed_and_argmax():
     V, d, M = 1000, 256, 9
     emb = _rand(V, d, scale=0.5, seed=14)
