@@ -43,8 +43,10 @@ class TPComm:
 
     # one-shot (every rank sends its partial to every rank) while a rank's
     # pushed bytes stay at or below this; two-shot (owner reduce, then
-    # broadcast) above
-    TWO_SHOT_BYTES = 4 << 20
+    # broadcast) above.  Measured crossover: one-shot faster at t = 2 with
+    # 1.3 MB pushed (M = 128, N = 5120), two-shot faster at t = 4 with 3.9 MB
+    # and at t = 2 with 5.2 MB
+    TWO_SHOT_BYTES = 2 << 20
 
     def __init__(self, rank: int, world: int, device, n_cols: int, max_rows: int = 16384,
                  group=None, handles_fn=None):
